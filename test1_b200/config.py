@@ -1,0 +1,144 @@
+"""SlideFSDPConfig: every knob of the layer-sliding trainer.
+
+Same field names, defaults, accepted values and validation messages as the
+reference's configuration dataclass (config.py:17-165 in LaiHOLA/Test1), so
+JSON configs written for the reference load unchanged.  Fields that the
+reference accepts but ignores (``prefetch_layers``, ``max_workers``,
+``clip_grad_norm``) are honoured here.
+
+Extra fields (all optional, reference configs never set them):
+    optimizer_sharding: "rank" (each rank updates 1/N of every layer, the
+        default) or "rank0" (the reference's single-optimizer placement).
+    fused_comm: use the fused NVLink kernels for shard all-gather and
+        gpu_reduce reduce-scatter when available (else NCCL).
+    host_threads: size of the per-rank host worker pool (0 = all CPUs in the
+        affinity mask).
+    use_native_kernels: run the model on the sm_100a kernels (True) or on
+        plain PyTorch ops (False; the CPU test path).
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass, fields
+from typing import Optional, Tuple
+
+import torch
+
+
+@dataclass
+class SlideFSDPConfig:
+    # Basic configuration
+    dtype: torch.dtype = torch.bfloat16
+    device: Optional[torch.device] = None  # auto-detect from LOCAL_RANK
+
+    # Parameter transfer strategy: "full" | "shard"
+    param_transfer_mode: str = "full"
+
+    # Gradient synchronization strategy: "gpu_reduce" | "cpu_reduce"
+    grad_sync_mode: str = "gpu_reduce"
+
+    # Optimizer configuration
+    lr: float = 1e-5
+    weight_decay: float = 0.01
+    adam_betas: Tuple[float, float] = (0.9, 0.999)
+    adam_eps: float = 1e-8
+    bias_correction: bool = True
+
+    # Runtime configuration
+    prefetch_layers: int = 1
+    max_workers: int = 1
+    enable_activation_checkpoint: bool = True
+    gpu_buffer_pool_size: int = 2
+
+    # Model / training configuration (used by train.py)
+    model_path: str = ""
+    max_seq_length: int = 1024
+    train_batch_size: int = 4
+    num_epochs: int = 1
+    log_every_n_steps: int = 1
+    seed: int = 42
+    use_liger_kernel: bool = True
+    attention_implementation: str = "flash_attention_2"
+
+    # Activation checkpoint offload: "cpu" | "nvme" | "none"
+    ac_offload_mode: str = "cpu"
+    ac_offload_dir: str = "/tmp/ac_offload"
+
+    # NVMe offload for optimizer states (fraction of each layer's state)
+    optimizer_nvme_offload_fraction: float = 0.0
+    optimizer_offload_dir: str = "/tmp/opt_offload"
+
+    # Gradient clipping (<= 0 disables)
+    clip_grad_norm: float = 1.0
+
+    # ---- fields without a reference counterpart --------------------------
+    optimizer_sharding: str = "rank"
+    fused_comm: bool = True
+    host_threads: int = 0
+    use_native_kernels: Optional[bool] = None  # None: native iff device is CUDA
+
+    def __post_init__(self):
+        if self.param_transfer_mode not in ("full", "shard"):
+            raise ValueError(
+                f"param_transfer_mode must be 'full' or 'shard', got {self.param_transfer_mode}"
+            )
+        if self.grad_sync_mode not in ("gpu_reduce", "cpu_reduce"):
+            raise ValueError(
+                f"grad_sync_mode must be 'gpu_reduce' or 'cpu_reduce', got {self.grad_sync_mode}"
+            )
+        if self.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+            raise ValueError(f"dtype must be torch.bfloat16 or torch.float16, got {self.dtype}")
+        if self.device is None:
+            local_rank = int(os.environ.get("LOCAL_RANK", 0))
+            self.device = torch.device("cuda", local_rank)
+        elif isinstance(self.device, str):
+            self.device = torch.device(self.device)
+        if self.ac_offload_mode not in ("cpu", "nvme", "none"):
+            raise ValueError(
+                f"ac_offload_mode must be 'cpu', 'nvme', or 'none', got {self.ac_offload_mode}"
+            )
+        if self.optimizer_sharding not in ("rank", "rank0"):
+            raise ValueError(
+                f"optimizer_sharding must be 'rank' or 'rank0', got {self.optimizer_sharding}"
+            )
+        if self.gpu_buffer_pool_size < 2:
+            raise ValueError("gpu_buffer_pool_size must be >= 2 (current layer + prefetched layer)")
+        if not 0.0 <= self.optimizer_nvme_offload_fraction <= 1.0:
+            raise ValueError("optimizer_nvme_offload_fraction must be in [0, 1]")
+        if isinstance(self.adam_betas, list):
+            self.adam_betas = tuple(self.adam_betas)
+        if self.use_native_kernels is None:
+            self.use_native_kernels = self.device.type == "cuda"
+
+    @classmethod
+    def from_dict(cls, config_dict: dict) -> "SlideFSDPConfig":
+        """Create a config from a dict (e.g. a JSON file).  Unknown keys are
+        dropped, as in the reference."""
+        d = dict(config_dict)
+        if "dtype" in d and isinstance(d["dtype"], str):
+            dtype_map = {
+                "bf16": torch.bfloat16,
+                "bfloat16": torch.bfloat16,
+                "fp16": torch.float16,
+                "float16": torch.float16,
+                "fp32": torch.float32,
+                "float32": torch.float32,
+            }
+            d["dtype"] = dtype_map.get(d["dtype"].lower(), torch.bfloat16)
+        if "device" in d and isinstance(d["device"], str):
+            d["device"] = torch.device(d["device"])
+        if "adam_betas" in d and isinstance(d["adam_betas"], list):
+            d["adam_betas"] = tuple(d["adam_betas"])
+        valid = {f.name for f in fields(cls)}
+        return cls(**{k: v for k, v in d.items() if k in valid})
+
+    def to_dict(self) -> dict:
+        out = {}
+        for f in fields(self):
+            value = getattr(self, f.name)
+            if isinstance(value, torch.dtype):
+                value = str(value).replace("torch.", "")
+            elif isinstance(value, torch.device):
+                value = str(value)
+            out[f.name] = value
+        return out

@@ -1,0 +1,35 @@
+// Portable fallback of the host kernels (one float per "vector").
+#define T1H_ISA scalar
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "host_kernels.h"
+
+namespace t1h {
+namespace scalar {
+struct V {
+  static constexpr int W = 1;
+  using R = float;
+  static inline R zero() { return 0.0f; }
+  static inline R set1(float x) { return x; }
+  static inline R add(R a, R b) { return a + b; }
+  static inline R mul(R a, R b) { return a * b; }
+  static inline R fmadd(R a, R b, R c) { return fmaf(a, b, c); }
+  static inline R sqrt(R a) { return sqrtf(a); }
+  static inline R div(R a, R b) { return a / b; }
+  static inline double hsum(R a) { return a; }
+  template <int DT, class T> static inline R ld(const T* p);
+  template <int DT, class T> static inline void st(T* p, R x);
+};
+}  // namespace scalar
+}  // namespace t1h
+
+#include "host_kernels.inl"
+
+namespace t1h {
+namespace scalar {
+template <int DT, class T> inline float V::ld(const T* p) { return Elem<DT>::ld(p); }
+template <int DT, class T> inline void V::st(T* p, float x) { Elem<DT>::st(p, x); }
+}  // namespace scalar
+}  // namespace t1h
