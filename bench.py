@@ -1,0 +1,298 @@
+"""Headline benchmark: Llama-3.1-8B-architecture layer-sliding training,
+tokens/s over all GPUs (device-timed, max over ranks).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+Config: Llama-3.1-8B architecture, random-init N(0,0.02)
+weights, fp32 master + fp32 Adam state in pinned host memory, bf16 compute,
+param_transfer_mode=full, grad_sync_mode=gpu_reduce, gpu_buffer_pool_size=2,
+per-GPU batch 4 x 1024 uniform-random tokens, causal LM loss.  Every timed
+step runs the full forward, backward and the host AdamW update of all 8.03 B
+parameters.  The weights streamed through the GPU each step (about 30 GB of
+host-to-device copies) exceed the 126 MB L2 many times over, so no L2 flush
+is inserted.
+
+Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "Llama-3.1-8B-arch tokens/sec, device-timed max over ranks, at 1/2/4/8 B200"
+BASELINE_VALUE = None  # BASELINE.md publishes no number
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=4)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--model", default="llama31_8b", choices=["llama31_8b", "tiny", "llama_70b"])
+    p.add_argument("--batch", type=int, default=4)
+    p.add_argument("--seq", type=int, default=1024)
+    p.add_argument("--param-transfer-mode", default="full", choices=["full", "shard"])
+    p.add_argument("--grad-sync-mode", default="gpu_reduce", choices=["gpu_reduce", "cpu_reduce"])
+    p.add_argument("--pool", type=int, default=2)
+    p.add_argument("--ac-offload", default="cpu", choices=["cpu", "nvme", "none"])
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--profile-json", default="")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def init_dist(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def run_ours(args, rank, world, local):
+    import torch
+
+    from test1_b200 import SlideFSDPConfig
+    from test1_b200.models.llama import LlamaConfig, LlamaForCausalLM
+    from test1_b200.slide_fsdp import SlideFSDP
+    from test1_b200.ops import native_launch_count
+
+    dev = torch.device("cuda", local)
+    mcfg = getattr(LlamaConfig, args.model)()
+    model = LlamaForCausalLM(mcfg, device="meta")
+    cfg = SlideFSDPConfig(dtype=torch.bfloat16, device=dev,
+                          param_transfer_mode=args.param_transfer_mode,
+                          grad_sync_mode=args.grad_sync_mode, gpu_buffer_pool_size=args.pool,
+                          lr=1e-5, weight_decay=0.01, ac_offload_mode=args.ac_offload,
+                          max_seq_length=args.seq, train_batch_size=args.batch, seed=42)
+    t0 = time.time()
+    engine = SlideFSDP(model, cfg)
+    init_s = time.time() - t0
+
+    V = mcfg.vocab_size
+    g = torch.Generator().manual_seed(1000 + rank)
+    n_batches = args.warmup + 2 * args.steps
+    batches = [torch.randint(0, V, (args.batch, args.seq), generator=g).pin_memory() for _ in range(n_batches)]
+    dev_batches = [b.to(dev) for b in batches]
+    torch.cuda.synchronize()
+
+    losses = []
+    # warm-up (untimed)
+    for i in range(args.warmup):
+        out = engine(input_ids=dev_batches[i], labels=dev_batches[i])
+        losses.append(float(out.loss))
+    engine.wait_for_updates()
+    barrier(world)
+
+    # ---- device-timed loop: inputs pre-staged on the device
+    sampler = ClockSampler(local)
+    sampler.start()
+    launches0 = native_launch_count()
+    h2d0 = engine.h2d_bytes
+    adam0 = engine.updates.busy_s
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    start.record()
+    last = None
+    for k in range(args.steps):
+        b = dev_batches[args.warmup + k]
+        last = engine(input_ids=b, labels=b).loss
+    engine.wait_for_updates()
+    end.record()
+    end.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    launches = native_launch_count() - launches0
+    dev_ms = start.elapsed_time(end)
+    dev_ms = max_over_ranks(dev_ms, world)
+    losses.append(float(last))
+    h2d_per_step = (engine.h2d_bytes - h2d0) / args.steps
+    adam_busy = (engine.updates.busy_s - adam0) / args.steps
+
+    # ---- end-to-end loop through the public API: pinned host batch copied
+    # in every step, loss read back every step
+    e2e = None
+    if not args.no_e2e:
+        barrier(world)
+        t0 = time.perf_counter()
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_end = torch.cuda.Event(enable_timing=True)
+        e_start.record()
+        for k in range(args.steps):
+            hb = batches[args.warmup + args.steps + k]
+            ids = hb.to(dev, non_blocking=True)
+            out = engine(input_ids=ids, attention_mask=None, labels=ids)
+            losses.append(out.loss.item())
+        engine.wait_for_updates()
+        e_end.record()
+        e_end.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(e_start.elapsed_time(e_end), world)
+        tokens = args.batch * args.seq * world * args.steps
+        e2e = {"value": round(tokens / (e2e_ms / 1e3), 2), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(args.batch * args.seq * 8),
+               "d2h_bytes_per_step": 4,
+               "wall_s": round(time.perf_counter() - t0, 3)}
+    engine.close()
+    return {
+        "dev_ms": dev_ms, "e2e": e2e, "clocks": clocks, "launches": launches, "init_s": init_s,
+        "losses": losses, "h2d_gb_per_step": h2d_per_step / 1e9, "adam_busy_s_per_step": adam_busy,
+    }
+
+
+def run_reference(args, rank, world, local):
+    from baseline.reference_arm import run as ref_run
+
+    return ref_run(args, rank, world, local)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = init_dist(args)
+    import torch
+
+    if args.impl == "reference":
+        res = run_reference(args, rank, world, local)
+        if res.get("unavailable"):
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
+            return
+    else:
+        res = run_ours(args, rank, world, local)
+
+    tokens = args.batch * args.seq * world * args.steps
+    value = tokens / (res["dev_ms"] / 1e3)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(res["dev_ms"] / args.steps, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None if BASELINE_VALUE is None else round(value / BASELINE_VALUE, 4),
+        "dtype": "bf16",
+        "data": "synthetic uniform-random tokens, random-init N(0,0.02) weights",
+        "config": {
+            "model": "Llama-3.1-8B architecture" if args.model == "llama31_8b" else args.model,
+            "global_batch": args.batch * world, "seq_len": args.seq,
+            "parallelism": f"dp{world}",
+            "param_transfer_mode": args.param_transfer_mode, "grad_sync_mode": args.grad_sync_mode,
+            "gpu_buffer_pool_size": args.pool, "ac_offload_mode": args.ac_offload,
+            "l2": "no flush: ~30 GB of weights stream host->device per step (>> 126 MB L2)",
+        },
+        "clocks": res.get("clocks"),
+        "e2e": res.get("e2e"),
+        "gpu_launches": res.get("launches"),
+    }
+    if args.impl == "reference":
+        line["impl"] = "reference"
+    extra = {k: res[k] for k in ("init_s", "h2d_gb_per_step", "adam_busy_s_per_step", "losses") if k in res}
+    line["detail"] = extra
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+        if args.profile_json:
+            with open(args.profile_json, "w") as f:
+                json.dump(line, f, indent=2)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -54,7 +54,6 @@ def cuda_extension():
         sources=sources,
         include_dirs=[os.path.join(ROOT, CUDA_DIR)],
         extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": nvcc_flags},
-        libraries=["cuda"],
     )
 
 

@@ -1,0 +1,42 @@
+// Python bindings of the sm_100a kernel library (test1_b200._cuda).
+#include <torch/extension.h>
+
+#include <unordered_map>
+
+namespace t1 {
+int64_t& launch_counter() {
+  static int64_t n = 0;
+  return n;
+}
+
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
+std::vector<torch::Tensor> rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w,
+                                       torch::Tensor rstd, c10::optional<torch::Tensor> resid);
+void rope_qkv(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D, torch::Tensor cos_t,
+              torch::Tensor sin_t, int64_t S, bool inverse);
+torch::Tensor swiglu_fwd(torch::Tensor gu);
+torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu);
+torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w);
+void embedding_bwd(torch::Tensor dh, torch::Tensor ids, torch::Tensor dw);
+std::vector<torch::Tensor> cross_entropy_fwd_bwd(torch::Tensor logits, torch::Tensor targets,
+                                                 int64_t ignore_index, double grad_scale);
+void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, bool b_mn,
+               c10::optional<torch::Tensor> R);
+int64_t gemm_check_error(bool reset);
+}  // namespace t1
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "test1_b200 sm_100a kernels";
+  m.def("launch_count", [] { return t1::launch_counter(); });
+  m.def("rmsnorm_fwd", &t1::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &t1::rmsnorm_bwd);
+  m.def("rope_qkv", &t1::rope_qkv);
+  m.def("swiglu_fwd", &t1::swiglu_fwd);
+  m.def("swiglu_bwd", &t1::swiglu_bwd);
+  m.def("embedding_fwd", &t1::embedding_fwd);
+  m.def("embedding_bwd", &t1::embedding_bwd);
+  m.def("cross_entropy_fwd_bwd", &t1::cross_entropy_fwd_bwd);
+  m.def("gemm_bf16", &t1::gemm_bf16, pybind11::arg("A"), pybind11::arg("B"), pybind11::arg("C"),
+        pybind11::arg("a_mn"), pybind11::arg("b_mn"), pybind11::arg("R") = pybind11::none());
+  m.def("gemm_check_error", &t1::gemm_check_error, pybind11::arg("reset") = false);
+}

@@ -1,0 +1,410 @@
+// Persistent bf16 GEMM on the 5th-generation tensor cores (tcgen05) for
+// sm_100a.
+//
+//   C[M, N] (bf16, row stride ldc) = A[M, K] * B[N, K]^T  (+ R[M, N])
+//
+// A and B are each either K-major (rows contiguous along K) or MN-major
+// (stored transposed, contiguous along M / N), which covers the three
+// products of a linear layer without any transpose copies:
+//   forward  y  = x  W^T : A = x  [T, K] K-major,    B = W [N, K] K-major
+//   dgrad    dx = dy W   : A = dy [T, N] K-major,    B = W stored [N, K] -> MN-major
+//   wgrad    dW = dy^T x : A = dy stored [T, N] -> MN-major, B = x stored [T, K] -> MN-major
+//
+// Structure (one CTA per SM, 192 threads, warp-specialised):
+//   warp 0     TMA producer: 128B-swizzled tiles of A (128 x 64) and B
+//              (256 x 64) into a 4-stage shared-memory ring, completion
+//              tracked by mbarriers (byte counts).  No multicast.
+//   warp 1     allocates 512 TMEM columns; one thread issues
+//              tcgen05.mma (M=128, N=256, K=16) into one of two 128x256 fp32
+//              TMEM accumulators and commits stage-release / tile-ready
+//              barriers.
+//   warps 2-5  epilogue: tcgen05.ld the finished accumulator (each warp owns
+//              its 32-lane TMEM quarter = 32 rows), optional residual add,
+//              bf16 rounding, 16-byte global stores; then hand the
+//              accumulator back, so tile i's epilogue overlaps tile i+1's
+//              MMAs.
+// Tiles are visited in grouped (GROUP_M) raster order for L2 reuse.  All
+// barrier waits are bounded (see sm100.cuh); a timeout writes a code to the
+// error word and the CTA unwinds.
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace t1 {
+
+using bf16 = __nv_bfloat16;
+using namespace sm100;
+
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 16;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+
+enum Epilogue : int { kStore = 0, kAddResidual = 1 };
+
+struct Params {
+  int M, N, K;
+  bf16* C;
+  long ldc;
+  const bf16* R;
+  long ldr;
+  int tiles_m, tiles_n, num_tiles, k_blocks;
+  int* err;
+};
+
+__device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
+  const int group = GROUP_M * tiles_n;
+  const int gid = tile / group;
+  const int first_m = gid * GROUP_M;
+  const int gsz = min(tiles_m - first_m, GROUP_M);
+  const int in_group = tile % group;
+  mb = first_m + in_group % gsz;
+  nb = in_group / gsz;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a,
+                     const __grid_constant__ CUtensorMap tma_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const ErrorSlot err{p.err};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tma_a);
+    prefetch_tensormap(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed_parity[STAGES];
+      bool armed[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) armed[s] = false;
+      for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
+        int mb, nb;
+        raster(tile, p.tiles_m, p.tiles_n, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            err.set(101);
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          armed[stage] = true;
+          armed_parity[stage] = phase;
+          uint8_t* a = sA + stage * A_BYTES;
+          uint8_t* b = sB + stage * B_BYTES;
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d(a, &tma_a, &full[stage], k0, mb * BM);
+          } else {
+            tma_load_2d(a, &tma_a, &full[stage], mb * BM, k0);
+            tma_load_2d(a + 8192, &tma_a, &full[stage], mb * BM + 64, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(b, &tma_b, &full[stage], k0, nb * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b + j * 8192, &tma_b, &full[stage], nb * BN + 64 * j, k0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // On abort, let every load this thread issued land before the CTA
+      // exits (each wait is itself bounded).
+      if (*abort_flag) {
+        for (int s = 0; s < STAGES; ++s)
+          if (armed[s]) mbar_wait(&full[s], armed_parity[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
+          err.set(102);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) {
+            err.set(103);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            mma_bf16(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (*abort_flag) break;
+      if (!mbar_wait(&tfull[acc], acc_phase)) {
+        err.set(104);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      int mb, nb;
+      raster(tile, p.tiles_m, p.tiles_n, mb, nb);
+      const int row = mb * BM + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      bf16* crow = p.C + static_cast<long>(row) * p.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c, r);
+        tmem_ld_wait();
+        const int col0 = nb * BN + c;
+        if (row_ok) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int col = col0 + 8 * v;
+            if (col < p.N) {
+              float f[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);
+              if (EPI == kAddResidual) {
+                float rv[8];
+                load8(p.R + static_cast<long>(row) * p.ldr + col, rv);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) f[j] += rv[j];
+              }
+              store8(crow + col, f);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gemm
+
+// ================================================================ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    T1_CHECK_CUDA(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                                   cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr != nullptr,
+                "cuTensorMapEncodeTiled not available from the driver");
+    return reinterpret_cast<EncodeTiledFn>(ptr);
+  }();
+  return fn;
+}
+
+// 2-D bf16 tensor map, 128B swizzle: `inner` contiguous elements per row,
+// `outer` rows, `ld` elements between rows, box = 64 x box_outer.
+static CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld,
+                            int box_outer) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "GEMM operand must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "GEMM operand row stride must be a multiple of 8 elements");
+  TORCH_CHECK(inner % 8 == 0, "GEMM operand contiguous extent must be a multiple of 8");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with ", (int)r);
+  return m;
+}
+
+torch::Tensor& gemm_error_word() {
+  static thread_local std::unordered_map<int, torch::Tensor> words;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto it = words.find(dev);
+  if (it == words.end()) {
+    auto t = torch::zeros({1}, torch::TensorOptions().dtype(torch::kInt32).device(torch::kCUDA, dev));
+    it = words.emplace(dev, t).first;
+  }
+  return it->second;
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p) {
+  auto kern = gemm::gemm_bf16_kernel<A_MN, B_MN, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gemm::SMEM_BYTES));
+    configured = true;
+  }
+  const int grid = std::min(p.num_tiles, num_sms());
+  kern<<<grid, 192, gemm::SMEM_BYTES, stream()>>>(ta, tb, p);
+  check_launch("gemm_bf16");
+  count_launch();
+}
+
+// C = A * B^T (+ R).  Logical shapes: A [M, K], B [N, K].  `a_mn` /
+// `b_mn` say the operand is stored transposed ([K, M] / [K, N], row-major).
+void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, bool b_mn,
+               c10::optional<torch::Tensor> R) {
+  T1_CHECK_INPUT(A, torch::kBFloat16);
+  T1_CHECK_INPUT(B, torch::kBFloat16);
+  T1_CHECK_INPUT(C, torch::kBFloat16);
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "2-D operands expected");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "row-major operands expected");
+  const int64_t M = a_mn ? A.size(1) : A.size(0);
+  const int64_t K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0);
+  const int64_t KB = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == KB, "GEMM reduction extents differ: ", K, " vs ", KB);
+  TORCH_CHECK(C.size(0) == M && C.size(1) == N, "C must be [", M, ", ", N, "]");
+  TORCH_CHECK(N % 8 == 0 && (C.stride(0) % 8) == 0, "N and ldc must be multiples of 8");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0, "C must be 16-byte aligned");
+  if (M == 0 || N == 0) return;
+  if (K == 0) {
+    if (R.has_value() && R->defined()) C.copy_(*R);
+    else C.zero_();
+    return;
+  }
+  CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), 64)
+                        : make_map(A.data_ptr(), K, M, A.stride(0), gemm::BM);
+  CUtensorMap tb = b_mn ? make_map(B.data_ptr(), N, K, B.stride(0), 64)
+                        : make_map(B.data_ptr(), K, N, B.stride(0), gemm::BN);
+  gemm::Params p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = reinterpret_cast<bf16*>(C.data_ptr());
+  p.ldc = C.stride(0);
+  p.R = nullptr;
+  p.ldr = 0;
+  p.tiles_m = (M + gemm::BM - 1) / gemm::BM;
+  p.tiles_n = (N + gemm::BN - 1) / gemm::BN;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.k_blocks = (K + gemm::BK - 1) / gemm::BK;
+  p.err = gemm_error_word().data_ptr<int>();
+  const bool add = R.has_value() && R->defined();
+  if (add) {
+    T1_CHECK_INPUT(*R, torch::kBFloat16);
+    TORCH_CHECK(R->size(0) == M && R->size(1) == N && R->stride(1) == 1, "residual must be [M, N]");
+    TORCH_CHECK(R->stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(R->data_ptr()) % 16 == 0,
+                "residual must be 16-byte aligned rows");
+    p.R = reinterpret_cast<const bf16*>(R->data_ptr());
+    p.ldr = R->stride(0);
+  }
+  if (!a_mn && !b_mn) {
+    if (add) launch<false, false, gemm::kAddResidual>(ta, tb, p);
+    else launch<false, false, gemm::kStore>(ta, tb, p);
+  } else if (!a_mn && b_mn) {
+    TORCH_CHECK(!add, "residual epilogue is only built for the forward layout");
+    launch<false, true, gemm::kStore>(ta, tb, p);
+  } else if (a_mn && b_mn) {
+    TORCH_CHECK(!add, "residual epilogue is only built for the forward layout");
+    launch<true, true, gemm::kStore>(ta, tb, p);
+  } else {
+    TORCH_CHECK(!add, "residual epilogue is only built for the forward layout");
+    launch<true, false, gemm::kStore>(ta, tb, p);
+  }
+}
+
+int64_t gemm_check_error(bool reset) {
+  auto& w = gemm_error_word();
+  int64_t v = w.item<int>();
+  if (reset) w.zero_();
+  return v;
+}
+
+}  // namespace t1

@@ -1,0 +1,703 @@
+"""SlideFSDP: layer-sliding training with host-resident master weights.
+
+Public API of the reference (slide_fsdp.py:116-745): ``SlideFSDP(model,
+config)``; ``forward(input_ids, attention_mask=None, labels=None)`` runs the
+forward pass *and* the backward pass and the per-layer optimizer updates,
+and returns a ``CausalLMOutputWithPast``; ``update_learning_rate``,
+``clip_grad_norm_``, ``save_pretrained``.  Added: ``save_state`` /
+``load_state`` (fp32 master + optimizer state + step counters, which the
+reference cannot save), ``close``.
+
+Layer indexing is the reference's: 0 = embedding, 1..L = decoder layers,
+L+1 = output layer (final norm + lm_head).
+
+How a step runs (all GPU work is ordered by CUDA events; the host blocks only
+on data dependencies):
+
+  forward   for each layer: the copy stream loads layer i+1 into a free pool
+            unit while layer i computes; the input of every decoder layer is
+            checkpointed (kept, or offloaded to host memory on a side
+            stream); the output layer computes loss and its own gradients in
+            one pass (no logits kept for a later backward).
+  backward  layers L..1 recompute from their checkpoint and run their
+            explicit backward kernels; parameter gradients land in the pool
+            unit; the gradient stream moves this rank's share to host memory
+            (reduce-scatter / device-to-host copy, see parallel/comm.py); the
+            host optimizer thread updates the shared fp32 master and writes
+            the bf16 shadow that the next forward copies to the GPU.
+
+Compared with the reference: no autograd hooks or per-layer autograd
+Functions (so no hook-ordering races, survey of slide_fsdp.py:416-430), no
+per-pass fp32->bf16 CPU cast (the optimizer writes the shadow), the embedding
+backward does not reload the embedding weights, and the optimizer is sharded
+across ranks.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import time
+import uuid
+from dataclasses import dataclass
+from typing import Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from . import _native, ops
+from .config import SlideFSDPConfig
+from .models.llama import LlamaConfig, LlamaDecoderLayer, LlamaForCausalLM, make_context
+from .optim.layer_adam import LayerAdam
+from .parallel.comm import CpuReduceSlots, make_comm
+from .runtime.activations import ActivationStore
+from .runtime.device import Event, Stream
+from .runtime.host_memory import HostRegion, RegionPlanner
+from .runtime.layer_state import (LayerBufferPool, LayerLayout, LayerRuntimeState, build_layout,
+                                  shard_size)
+from .runtime.update import UpdateScheduler
+
+try:
+    from transformers.modeling_outputs import CausalLMOutputWithPast
+except Exception:  # pragma: no cover
+    @dataclass
+    class CausalLMOutputWithPast:  # type: ignore[no-redef]
+        loss: Optional[torch.Tensor] = None
+        logits: Optional[torch.Tensor] = None
+
+
+class OutputLayer(nn.Module):
+    """Final norm + lm_head moved as one unit (reference slide_fsdp.py:45-113).
+    ``named_parameters``: norm.weight, lm_head.weight."""
+
+    def __init__(self, norm: nn.Module, lm_head: nn.Module, eps: float):
+        super().__init__()
+        self.norm = norm
+        self.lm_head = lm_head
+        self.eps = eps
+
+    def _grads(self):
+        for p in self.parameters():
+            if p.grad is None:
+                p.grad = torch.zeros_like(p)
+        return self.norm.weight.grad, self.lm_head.weight.grad
+
+    def loss_and_grad(self, h: torch.Tensor, ctx):
+        """Forward + loss + backward of this layer.  Returns (loss, dh)."""
+        w_n, w_lm = self.norm.weight.data, self.lm_head.weight.data
+        x, rstd = ops.rmsnorm_fwd(h, w_n, self.eps)
+        logits = ops.linear_fwd(x, w_lm)
+        loss, dlogits, _ = ops.cross_entropy_fwd_bwd(logits, ctx.targets)
+        del logits
+        g_n, g_lm = self._grads()
+        dx = ops.linear_dgrad(dlogits, w_lm)
+        ops.linear_wgrad(dlogits, x, out=g_lm)
+        del dlogits
+        dh, dw = ops.rmsnorm_bwd(dx, h, w_n, rstd)
+        g_n.copy_(dw)
+        return loss, dh
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        x, _ = ops.rmsnorm_fwd(h, self.norm.weight.data, self.eps)
+        return ops.linear_fwd(x, self.lm_head.weight.data)
+
+
+def _convert_hf_llama(model: nn.Module) -> LlamaForCausalLM:
+    """Build our Llama module from an HF LlamaForCausalLM, copying weights
+    (names are identical)."""
+    cfg = LlamaConfig.from_hf(model.config)
+    ours = LlamaForCausalLM(cfg, device="meta")
+    src = dict(model.named_parameters())
+    for name, p in ours.named_parameters():
+        if name not in src:
+            raise ValueError(f"HF model lacks parameter {name}")
+        if tuple(src[name].shape) != tuple(p.shape):
+            raise ValueError(f"shape mismatch for {name}: {tuple(src[name].shape)} vs {tuple(p.shape)}")
+        p.data = src[name].data
+    return ours
+
+
+class SlideFSDP(nn.Module):
+    def __init__(self, model: nn.Module, config: SlideFSDPConfig):
+        super().__init__()
+        self.config = config
+        self.device = torch.device(config.device)
+        self.dtype = config.dtype
+        self.rank = dist.get_rank() if dist.is_initialized() else 0
+        self.world_size = dist.get_world_size() if dist.is_initialized() else 1
+        self.is_cuda = self.device.type == "cuda"
+        if self.is_cuda:
+            torch.cuda.set_device(self.device)
+        _native.host()  # load + size the host worker pool
+        if config.host_threads > 0:
+            _native.host().configure_threads(config.host_threads, _native._cpu_list_from_env())
+
+        if not isinstance(model, LlamaForCausalLM):
+            if getattr(getattr(model, "config", None), "model_type", None) in ("llama", "mistral"):
+                model = _convert_hf_llama(model)
+            else:
+                raise NotImplementedError(
+                    f"SlideFSDP supports Llama-architecture causal LMs; got {type(model).__name__}")
+        if model.config.tie_word_embeddings:
+            raise NotImplementedError("tied input/output embeddings are not supported by layer sliding")
+        self.base_model = model
+        self.model_config = model.config
+        self._split_model(model)
+
+        # ---- communication -------------------------------------------------
+        self.comm = None  # built after the shared region exists (cpu_reduce slots live there)
+        self._session = self._make_session_id()
+
+        # ---- layouts -------------------------------------------------------
+        self.layouts: List[LayerLayout] = []
+        for idx, (kind, mod) in enumerate(self._layer_modules()):
+            self.layouts.append(build_layout(idx, kind, mod))
+        self.num_layers = len(self.layouts)
+        self.total_params = sum(l.numel for l in self.layouts)
+        self.max_param_size = max(l.numel for l in self.layouts)
+
+        # ---- shared host region: counters | master fp32 | shadow bf16 | cpu slots
+        plan = RegionPlanner(align=4096)
+        n_counters = 4 * self.num_layers + 64
+        self._ctr_off = plan.take(8 * n_counters)
+        for l in self.layouts:
+            l.master_off = plan.take(4 * l.numel)
+        for l in self.layouts:
+            l.shadow_off = plan.take(2 * l.numel)
+        dec_caps = [l.numel for l in self.layouts if l.kind == "decoder"]
+        big_caps = [l.numel for l in self.layouts if l.kind != "decoder"]
+        self._slot_cap = max(dec_caps + big_caps)
+        self._n_slots = 4
+        self._slots_off = None
+        if self.world_size > 1 and config.grad_sync_mode == "cpu_reduce":
+            self._slots_off = plan.take(CpuReduceSlots.region_bytes(self._slot_cap, self.world_size,
+                                                                    self._n_slots))
+        shm_path = None
+        if self.world_size > 1:
+            shm_path = f"/dev/shm/t1b200_{self._session}.bin"
+        creator = self.rank == 0
+        if self.world_size > 1 and not creator:
+            dist.barrier()
+        self.shared = HostRegion(plan.size, shm_path=shm_path, create=creator or shm_path is None,
+                                 pin=False)
+        if self.world_size > 1 and creator:
+            dist.barrier()
+        self.counters = self.shared.view(torch.uint8, self._ctr_off, 8 * n_counters)
+
+        # ---- comm strategy (needs the slot region for cpu_reduce)
+        cpu_slots = None
+        if self._slots_off is not None:
+            slot_region = _SubRegion(self.shared, self._slots_off)
+            cpu_slots = CpuReduceSlots(slot_region, self.counters, 2 * self.num_layers, self.num_layers,
+                                       self._slot_cap, self.rank, self.world_size, self._n_slots)
+        self.cpu_slots = cpu_slots
+        self.comm = make_comm(config, self.device, self.rank, self.world_size, cpu_slots)
+
+        # ---- master init (rank 0 writes), shadow cast, then everyone pins
+        self._init_master(model)
+        if self.world_size > 1:
+            dist.barrier()
+        if self.is_cuda:
+            self.shared.pin()
+
+        # ---- per-rank host gradients (this rank's update range of each layer)
+        gplan = RegionPlanner(align=4096)
+        self._grad_offs = []
+        for l in self.layouts:
+            s, e = self.comm.update_range(l.numel)
+            gbytes = torch.tensor([], dtype=self.dtype).element_size()
+            self._grad_offs.append((gplan.take(gbytes * max(e - s, 0)), max(e - s, 0)))
+        self.grad_region = HostRegion(max(gplan.size, 4096), pin=self.is_cuda)
+
+        # ---- runtime states
+        self.layer_states: List[LayerRuntimeState] = []
+        for l, (kind, mod) in zip(self.layouts, self._layer_modules()):
+            master = self.shared.view(torch.float32, l.master_off, l.numel)
+            shadow = self.shared.view(self.dtype if self.dtype != torch.float32 else torch.float32,
+                                      l.shadow_off, l.numel) if self.dtype != torch.float32 else None
+            goff, gn = self._grad_offs[l.idx]
+            grad_host = self.grad_region.view(self.dtype if self.dtype != torch.float32 else torch.float32,
+                                              goff, gn) if gn else None
+            st = LayerRuntimeState(l, mod, master, shadow if shadow is not None else master,
+                                   grad_host, self.comm.update_range(l.numel))
+            st.bind_host()
+            self.layer_states.append(st)
+
+        # ---- optimizer (this rank's range of every layer)
+        self.layer_optimizer = self._create_optimizer(config)
+
+        # ---- GPU buffer pools
+        self.pool = LayerBufferPool(max(self.comm.unit_capacity(c) for c in dec_caps) if dec_caps else 1,
+                                    self.dtype, self.device, config.gpu_buffer_pool_size, name="decoder-pool")
+        self.big_pool = LayerBufferPool(max(self.comm.unit_capacity(c) for c in big_caps),
+                                        self.dtype, self.device, 1, name="embed/output-unit")
+        for st in self.layer_states:
+            st.pool = self.pool if st.kind == "decoder" else self.big_pool
+
+        # ---- streams, scheduler, activations
+        self.h2d_stream = Stream(self.device)
+        self.grad_stream = Stream(self.device)
+        self.ac_d2h = Stream(self.device)
+        self.updates = UpdateScheduler(self.counters)
+        self._reducer = (UpdateScheduler(self.counters, name="t1-reduce", fifo=True)
+                         if cpu_slots is not None else None)
+        self.acts = ActivationStore(config.ac_offload_mode if config.enable_activation_checkpoint else "gpu",
+                                    self.device, self.ac_d2h, self.h2d_stream, config.ac_offload_dir)
+        self.completed_steps = 0
+        self.stats: Dict[str, float] = {}
+        self.h2d_bytes = 0
+        self.position_embeddings = None
+        self._closed = False
+        if self.rank == 0 and os.environ.get("T1_QUIET", "0") != "1":
+            self._print_model_info()
+
+    # ------------------------------------------------------------ set-up
+    def _make_session_id(self) -> str:
+        sid = [uuid.uuid4().hex[:12]]
+        if self.world_size > 1:
+            dist.broadcast_object_list(sid, src=0)
+        return sid[0]
+
+    def _split_model(self, model: LlamaForCausalLM) -> None:
+        decoder = model.get_decoder()
+        self.embed_tokens = model.get_input_embeddings()
+        self.decoder_layers = nn.ModuleList(decoder.layers)
+        self.num_decoder_layers = len(decoder.layers)
+        self.output_layer = OutputLayer(decoder.norm, model.get_output_embeddings(),
+                                        model.config.rms_norm_eps)
+
+    def _layer_modules(self):
+        out = [("embed", self.embed_tokens)]
+        out += [("decoder", l) for l in self.decoder_layers]
+        out.append(("output", self.output_layer))
+        return out
+
+    @property
+    def all_layers(self):
+        return [m for _, m in self._layer_modules()]
+
+    def _create_optimizer(self, config: SlideFSDPConfig) -> Optional[LayerAdam]:
+        opt = LayerAdam(lr=config.lr, betas=config.adam_betas, eps=config.adam_eps,
+                        weight_decay=config.weight_decay, bias_correction=config.bias_correction,
+                        adamw_mode=True, fp32_optimizer_state=True, num_layer=self.num_layers,
+                        nvme_offload_fraction=config.optimizer_nvme_offload_fraction,
+                        offload_dir=config.optimizer_offload_dir, prefetch=True)
+        n = 0
+        for st in self.layer_states:
+            s, e = st.shard
+            if e > s:
+                opt.add_flat_layer(st.idx, st.master[s:e])
+                n += 1
+        return opt if n else None
+
+    @torch.no_grad()
+    def _init_master(self, model: LlamaForCausalLM) -> None:
+        """Rank 0 fills the shared fp32 master from the model's parameters
+        (random N(0, initializer_range) when they are on the meta device),
+        then writes the low-precision shadow."""
+        if self.rank != 0:
+            return
+        host = _native.host()
+        std = self.model_config.initializer_range
+        seed = self.config.seed
+        gen_dev = self.device if self.is_cuda else torch.device("cpu")
+        for l in self.layouts:
+            master = self.shared.view(torch.float32, l.master_off, l.numel)
+            for k, e in enumerate(l.entries):
+                dst = master[e.offset:e.offset + e.numel]
+                p = e.param
+                if p.device.type == "meta":
+                    if e.name.endswith("norm.weight") or e.name.endswith("layernorm.weight"):
+                        dst.fill_(1.0)
+                    else:
+                        g = torch.Generator(device=gen_dev)
+                        g.manual_seed(seed * 1_000_003 + l.idx * 7919 + k)
+                        chunk = 1 << 26
+                        for c0 in range(0, e.numel, chunk):
+                            c1 = min(e.numel, c0 + chunk)
+                            r = torch.randn(c1 - c0, generator=g, device=gen_dev, dtype=torch.float32)
+                            dst[c0:c1].copy_(r.mul_(std))
+                else:
+                    dst.copy_(p.detach().reshape(-1).float())
+            if self.dtype != torch.float32:
+                shadow = self.shared.view(self.dtype, l.shadow_off, l.numel)
+                host.cast_(shadow, master, 1.0)
+
+    def _print_model_info(self) -> None:
+        gb = 1e9
+        print("=" * 60)
+        print("SlideFSDP (test1_b200) model info")
+        print("=" * 60)
+        print(f"Model type: {self.model_config.model_type}")
+        print(f"Num decoder layers: {self.num_decoder_layers}")
+        print(f"Total parameters: {self.total_params:,}")
+        print(f"Max layer param size: {self.max_param_size:,}")
+        print(f"Param transfer mode: {self.config.param_transfer_mode}")
+        print(f"Grad sync mode: {self.config.grad_sync_mode}  (optimizer sharding: {self.config.optimizer_sharding})")
+        print(f"World size: {self.world_size}   comm: {self.comm.name}")
+        print(f"Host memory: master {self.total_params * 4 / gb:.2f} GB, shadow {self.total_params * 2 / gb:.2f} GB, "
+              f"optimizer state (this rank) {self._opt_numel() * 8 / gb:.2f} GB")
+        print(f"GPU buffer pool: {self.config.gpu_buffer_pool_size} units x {self.pool.capacity:,} elements "
+              f"+ 1 embed/output unit x {self.big_pool.capacity:,}")
+        print(f"Host SIMD: {_native.host().simd_level()}  threads: {_native.host().num_threads()}")
+        print("=" * 60, flush=True)
+
+    def _opt_numel(self) -> int:
+        return sum(max(0, st.shard[1] - st.shard[0]) for st in self.layer_states)
+
+    # ------------------------------------------------------ layer movement
+    def _update_target(self) -> int:
+        return self.comm.updaters * self.completed_steps
+
+    def _fetch(self, st: LayerRuntimeState, with_grad: bool, need_weights: bool = True) -> None:
+        """Acquire a pool unit for ``st`` and enqueue its parameter load."""
+        if st.resident:
+            if with_grad:
+                st.bind_device(with_grad=True)
+            return
+        unit = st.pool.acquire(st.idx)
+        st.unit = unit
+        if need_weights:
+            # the previous step's optimizer update of this layer must be visible
+            self.updates.wait_counter(st.idx, self._update_target())
+            self.h2d_stream.wait(unit.free_event)
+            self.comm.fetch_params(st, unit.param, self.h2d_stream)
+            self.h2d_bytes += st.numel * unit.param.element_size()
+            st.loaded = self.h2d_stream.record()
+        else:
+            st.loaded = unit.free_event
+        st.bind_device(with_grad=with_grad)
+
+    def _wait_loaded(self, st: LayerRuntimeState) -> None:
+        if st.loaded is not None and st.loaded.e is not None:
+            torch.cuda.current_stream(self.device).wait_event(st.loaded.e)
+        st.loaded = None
+
+    def _release(self, st: LayerRuntimeState, done: Event) -> None:
+        st.pool.release(st.unit, done)
+        st.unit = None
+        st.bind_host()
+
+    def _offload_grads(self, st: LayerRuntimeState, step: int) -> None:
+        """After the backward of ``st``: move gradients to the host, free
+        the unit, schedule the optimizer update."""
+        computed = Event(self.device).record()
+        self.grad_stream.wait(computed)
+        unit = st.unit
+        self.comm.sync_grads(st, unit.grad, self.grad_stream)
+        ready = self.grad_stream.record()
+        self._release(st, ready)
+        self._schedule_update(st, ready, step)
+
+    def _schedule_update(self, st: LayerRuntimeState, ready: Event, step: int) -> None:
+        opt = self.layer_optimizer
+        s, e = st.shard
+        has_work = opt is not None and e > s
+        scale = self.comm.grad_scale
+        shadow = st.shadow[s:e] if (has_work and self.dtype != torch.float32) else None
+
+        def run_update(grad=None):
+            if has_work:
+                g = grad if grad is not None else st.grad_host
+                opt.step_flat(st.idx, g, shadow=shadow, grad_scale=scale)
+            self.updates.publish(st.idx)
+
+        if self._reducer is not None:
+            def run_reduce():
+                g = self.comm.host_reduce(st, step)
+                self.updates.submit(st.idx, None, lambda: run_update(g))
+            self._reducer.submit(st.idx, ready, run_reduce)
+        else:
+            self.updates.submit(st.idx, ready, run_update)
+
+    # -------------------------------------------------------------- step
+    def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None,
+                labels: Optional[torch.Tensor] = None, **kwargs) -> CausalLMOutputWithPast:
+        if attention_mask is not None:
+            self._check_mask(attention_mask)
+        if labels is None:
+            return CausalLMOutputWithPast(loss=None, logits=self._inference(input_ids))
+        loss = self._train_step(input_ids, labels)
+        return CausalLMOutputWithPast(loss=loss, logits=None)
+
+    def _check_mask(self, mask: torch.Tensor) -> None:
+        """Causal attention without a mask is exact for right padding (no
+        real token attends to a later pad token; pad positions carry label
+        -100).  Other masks are rejected."""
+        m = mask.bool()
+        if bool(m.all()):
+            return
+        # right padding: once a row turns False it stays False
+        if bool((m[:, 1:] & ~m[:, :-1]).any()):
+            raise NotImplementedError("only right-padded attention masks are supported")
+
+    @torch.no_grad()
+    def _train_step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        cfg = self.model_config
+        dev = self.device
+        step = self.completed_steps + 1
+        if self.cpu_slots is not None:
+            self.cpu_slots.step = step
+        ctx = make_context(cfg, input_ids, labels, dev)
+        S = self.layer_states
+        L = self.num_decoder_layers
+        emb, out = S[0], S[L + 1]
+
+        # ---------------- forward
+        self._fetch(emb, with_grad=False)
+        if L > 0:
+            self._fetch(S[1], with_grad=False)
+        self._wait_loaded(emb)
+        h = emb.module.forward_ids(ctx.input_ids)
+        self._release(emb, Event(dev).record())
+        prefetch = max(1, min(self.config.prefetch_layers, self.config.gpu_buffer_pool_size - 1))
+        saved_all = {}
+        for i in range(1, L + 1):
+            st = S[i]
+            self._wait_loaded(st)
+            if self.config.enable_activation_checkpoint:
+                self.acts.save(i, h, keep_on_gpu=(i == L))
+                h, _ = st.module.forward_train(h, ctx, save=False)
+            else:
+                h, saved_all[i] = st.module.forward_train(h, ctx, save=True)
+            # prefetch the next layer(s) into free units
+            for j in range(i + 1, min(i + prefetch, L) + 1):
+                if not S[j].resident and S[j].pool.num_free:
+                    self._fetch(S[j], with_grad=False)
+            if i == L:
+                self._fetch(out, with_grad=True)
+            else:
+                self._release(st, Event(dev).record())
+            if i + 1 <= L and not S[i + 1].resident:
+                self._fetch(S[i + 1], with_grad=False)
+        if L == 0:
+            self._fetch(out, with_grad=True)
+
+        # ---------------- output layer: loss + its backward
+        self._wait_loaded(out)
+        loss, dh = out.module.loss_and_grad(h, ctx)
+        del h
+        if L > 0:
+            S[L].bind_device(with_grad=True)
+        self._offload_grads(out, step)
+
+        # ---------------- backward through the decoder layers
+        for i in range(L, 0, -1):
+            st = S[i]
+            if i - 1 >= 1:
+                self._fetch(S[i - 1], with_grad=True)
+                if self.config.enable_activation_checkpoint:
+                    self.acts.prefetch(i - 1)
+            self._wait_loaded(st)
+            if self.config.enable_activation_checkpoint:
+                h_in = self.acts.get(i)
+                _, saved = st.module.forward_train(h_in, ctx, save=True)
+                del h_in
+            else:
+                saved = saved_all.pop(i)
+            dh = st.module.backward(saved, dh, ctx)
+            del saved
+            self._offload_grads(st, step)
+
+        # ---------------- embedding backward (weights not needed)
+        self._fetch(emb, with_grad=True, need_weights=False)
+        self._wait_loaded(emb)
+        emb.module.backward_ids(dh, ctx.input_ids)
+        del dh
+        self._offload_grads(emb, step)
+        self.acts.clear()
+        self.completed_steps = step
+        return loss
+
+    @torch.no_grad()
+    def _inference(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """Forward only; returns logits [B, S, V]."""
+        cfg = self.model_config
+        ctx = make_context(cfg, input_ids, None, self.device)
+        S = self.layer_states
+        L = self.num_decoder_layers
+        self._fetch(S[0], with_grad=False)
+        self._wait_loaded(S[0])
+        h = S[0].module.forward_ids(ctx.input_ids)
+        self._release(S[0], Event(self.device).record())
+        for i in range(1, L + 2):
+            st = S[i]
+            self._fetch(st, with_grad=False)
+            if i + 1 < L + 2 and S[i + 1].pool.num_free:
+                self._fetch(S[i + 1], with_grad=False)
+            self._wait_loaded(st)
+            if i <= L:
+                h = st.module(h, ctx)
+            else:
+                h = st.module.logits(h)
+            self._release(st, Event(self.device).record())
+        B, T = input_ids.shape
+        return h.view(B, T, -1)
+
+    # ------------------------------------------------------------ control
+    def wait_for_updates(self) -> None:
+        """Block until every scheduled optimizer update (all ranks) landed."""
+        if self._reducer is not None:
+            self._reducer.drain()
+        self.updates.drain()
+        for st in self.layer_states:
+            self.updates.wait_counter(st.idx, self._update_target())
+
+    def update_learning_rate(self, new_lr: float) -> None:
+        self.wait_for_updates()
+        self.config.lr = new_lr
+        if self.layer_optimizer is not None:
+            self.layer_optimizer.update_learning_rate(new_lr)
+
+    def clip_grad_norm_(self, max_norm: float) -> torch.Tensor:
+        """Global L2 norm of the last step's (averaged) gradients held in host
+        memory, summed over ranks' shards.  As in the reference, the fused
+        step has already applied the updates by the time this can run, so the
+        norm is reported and the held gradients are scaled in place but no
+        update is repeated."""
+        self.wait_for_updates()
+        host = _native.host()
+        sq = 0.0
+        scale2 = self.comm.grad_scale ** 2
+        for st in self.layer_states:
+            if st.grad_host is not None and st.grad_host.numel():
+                sq += host.sumsq(st.grad_host) * scale2
+        t = torch.tensor([sq], dtype=torch.float64, device=self.device)
+        if self.world_size > 1 and self.comm.updaters > 1:
+            dist.all_reduce(t)
+        total = math.sqrt(float(t.item()))
+        coef = max_norm / (total + 1e-6)
+        if coef < 1:
+            for st in self.layer_states:
+                if st.grad_host is not None and st.grad_host.numel():
+                    host.cast_(st.grad_host, st.grad_host, coef)
+        return torch.tensor(total)
+
+    # --------------------------------------------------------- persistence
+    def _gather_full_param(self, st: LayerRuntimeState) -> torch.Tensor:
+        return st.master  # shared host memory holds every rank's updates
+
+    def named_master_tensors(self):
+        """(HF name, fp32 host view) for every parameter, in model order."""
+        prefix = {"embed": "model.embed_tokens.", "output": ""}
+        out = []
+        for st in self.layer_states:
+            views = st.layout.views(st.master)
+            for e in st.layout.entries:
+                if st.kind == "embed":
+                    name = "model.embed_tokens." + e.name
+                elif st.kind == "output":
+                    name = ("model." + e.name) if e.name.startswith("norm.") else e.name
+                else:
+                    name = f"model.layers.{st.idx - 1}.{e.name}"
+                out.append((name, views[e.name]))
+        return out
+
+    def save_pretrained(self, output_dir: str) -> str:
+        """Write an HF-layout checkpoint (config.json + safetensors in
+        ``config.dtype``).  Unlike the reference (slide_fsdp.py:705-733) this
+        neither converts the live parameters nor stops training."""
+        from .utils.checkpoint_io import save_hf_checkpoint
+
+        self.wait_for_updates()
+        if self.rank == 0:
+            save_hf_checkpoint(output_dir, self.model_config.to_hf_dict(),
+                               dict(self.named_master_tensors()), self.dtype)
+            print(f"Model saved to {output_dir}")
+        if self.world_size > 1:
+            dist.barrier()
+        return output_dir
+
+    def save_state(self, directory: str) -> None:
+        """fp32 master (rank 0) + this rank's optimizer shards, one file per
+        layer index (``layer_<i>.pt`` / ``optim_rank<r>_layer_<i>.pt``) and a
+        JSON manifest.  ``load_state`` restores them exactly."""
+        self.wait_for_updates()
+        os.makedirs(directory, exist_ok=True)
+        if self.rank == 0:
+            for st in self.layer_states:
+                torch.save(st.master.clone(), os.path.join(directory, f"layer_{st.idx}.pt"))
+            with open(os.path.join(directory, "manifest.json"), "w") as f:
+                json.dump({"world_size": self.world_size, "completed_steps": self.completed_steps,
+                           "optimizer_sharding": self.config.optimizer_sharding,
+                           "num_layers": self.num_layers, "config": self.config.to_dict(),
+                           "model": self.model_config.to_hf_dict()}, f, indent=2, default=str)
+        if self.layer_optimizer is not None:
+            for st in self.layer_states:
+                if st.shard[1] > st.shard[0]:
+                    sd = self.layer_optimizer.state_dict_for_layer(st.idx)
+                    torch.save({"step": sd["step"], "exp_avg": sd["exp_avg"].clone(),
+                                "exp_avg_sq": sd["exp_avg_sq"].clone(), "shard": st.shard},
+                               os.path.join(directory, f"optim_rank{self.rank}_layer_{st.idx}.pt"))
+        if self.world_size > 1:
+            dist.barrier()
+
+    def load_state(self, directory: str) -> None:
+        self.wait_for_updates()
+        with open(os.path.join(directory, "manifest.json")) as f:
+            manifest = json.load(f)
+        if manifest["world_size"] != self.world_size:
+            raise ValueError("optimizer shards were saved with a different world size")
+        host = _native.host()
+        if self.rank == 0:
+            for st in self.layer_states:
+                st.master.copy_(torch.load(os.path.join(directory, f"layer_{st.idx}.pt")))
+                if self.dtype != torch.float32:
+                    host.cast_(st.shadow, st.master, 1.0)
+        if self.layer_optimizer is not None:
+            for st in self.layer_states:
+                if st.shard[1] > st.shard[0]:
+                    sd = torch.load(os.path.join(directory, f"optim_rank{self.rank}_layer_{st.idx}.pt"))
+                    if tuple(sd["shard"]) != tuple(st.shard):
+                        raise ValueError(f"shard mismatch for layer {st.idx}")
+                    self.layer_optimizer.load_state_for_layer(st.idx, sd)
+        # counters keep counting from here: completed_steps is the number of
+        # update rounds already published by this process group
+        if self.world_size > 1:
+            dist.barrier()
+
+    # --------------------------------------------------------------- misc
+    def step_stats(self) -> Dict[str, float]:
+        return {"h2d_bytes": float(self.h2d_bytes), "adam_busy_s": self.updates.busy_s,
+                "ac_d2h_bytes": float(self.acts.bytes_d2h), "ac_h2d_bytes": float(self.acts.bytes_h2d)}
+
+    def close(self) -> None:
+        if getattr(self, "_closed", True):
+            return
+        self._closed = True
+        try:
+            self.wait_for_updates()
+        except Exception:
+            pass
+        self.updates.close()
+        if self._reducer is not None:
+            self._reducer.close()
+        self.acts.close()
+        if self.layer_optimizer is not None:
+            self.layer_optimizer.close()
+        for st in self.layer_states:
+            for e in st.layout.entries:
+                e.param.data = torch.empty(0)
+                e.param.grad = None
+        if self.is_cuda:
+            torch.cuda.synchronize(self.device)
+        self.grad_region.close()
+        self.shared.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _SubRegion:
+    """A HostRegion view starting at a byte offset (for the cpu_reduce slots)."""
+
+    def __init__(self, region: HostRegion, base: int):
+        self.region = region
+        self.base = base
+
+    def view(self, dtype, offset_bytes, numel):
+        return self.region.view(dtype, self.base + offset_bytes, numel)

@@ -1,0 +1,143 @@
+"""sm_100a kernels vs fp32 PyTorch statements of the same ops (ops.reference)."""
+import math
+
+import pytest
+import torch
+
+from test1_b200.ops import native, reference as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _gemm_error_clean(cuda_device):
+    native.gemm_error(reset=True)
+    yield
+    torch.cuda.synchronize()
+    assert native.gemm_error(reset=True) == 0, "a bounded wait inside the GEMM expired"
+
+
+GEMM_SHAPES = [(128, 256, 64), (256, 512, 128), (300, 264, 200), (1000, 776, 520), (4096, 6144, 4096)]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm_forward_layout(M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    y = native.linear_fwd(x, w)
+    expect = x.float() @ w.float().t()
+    assert _rel(y, expect) < 6e-3
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES[:4])
+def test_gemm_residual(M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    r = torch.randn(M, N, device="cuda", generator=g).bfloat16() * 10
+    y = native.linear_fwd(x, w, residual=r)
+    expect = x.float() @ w.float().t() + r.float()
+    assert _rel(y, expect) < 6e-3
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm_dgrad_layout(M, N, K):
+    # dx [M, K] = dy [M, N] @ W [N, K]
+    g = torch.Generator(device="cuda").manual_seed(11)
+    dy = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    dx = native.linear_dgrad(dy, w)
+    assert _rel(dx, dy.float() @ w.float()) < 6e-3
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm_wgrad_layout(M, N, K):
+    # dW [N, K] = dy^T [N, M] @ x [M, K]
+    g = torch.Generator(device="cuda").manual_seed(13)
+    dy = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    out = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
+    native.linear_wgrad(dy, x, out=out)
+    assert _rel(out, dy.float().t() @ x.float()) < 6e-3
+
+
+def test_gemm_into_strided_output():
+    x = torch.randn(256, 512, device="cuda").bfloat16()
+    w = torch.randn(384, 512, device="cuda").bfloat16()
+    big = torch.zeros(256, 1024, device="cuda", dtype=torch.bfloat16)
+    native.gemm(x, w, big[:, 256:640])
+    assert _rel(big[:, 256:640], x.float() @ w.float().t()) < 6e-3
+    assert big[:, :256].abs().max().item() == 0 and big[:, 640:].abs().max().item() == 0
+
+
+@pytest.mark.parametrize("T,H", [(7, 256), (1024, 4096), (33, 8192)])
+def test_rmsnorm(T, H):
+    x = (torch.randn(T, H, device="cuda") * 3).bfloat16()
+    w = (torch.rand(H, device="cuda") + 0.5).bfloat16()
+    y, rstd = native.rmsnorm_fwd(x, w, 1e-5)
+    ye, re = ref.rmsnorm_fwd(x.float(), w.float(), 1e-5)
+    assert _rel(y, ye) < 5e-3
+    assert torch.allclose(rstd, re, rtol=1e-4)
+    dy = torch.randn(T, H, device="cuda").bfloat16()
+    res = torch.randn(T, H, device="cuda").bfloat16()
+    dx, dw = native.rmsnorm_bwd(dy, x, w, rstd, res)
+    dxe, dwe = ref.rmsnorm_bwd(dy.float(), x.float(), w.float(), re, res.float())
+    assert _rel(dx, dxe) < 5e-3
+    assert _rel(dw, dwe) < 5e-3
+
+
+def test_rope_qkv_roundtrip():
+    T, S, nq, nkv, D = 512, 256, 8, 2, 128
+    cos, sin = ref.rope_tables(D, S, 500000.0, {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                                "high_freq_factor": 4.0,
+                                                "original_max_position_embeddings": 8192}, "cuda")
+    qkv = torch.randn(T, (nq + 2 * nkv) * D, device="cuda").bfloat16()
+    expect = ref.rope_qkv_(qkv.float().clone(), nq, nkv, D, cos, sin, S)
+    got = native.rope_qkv_(qkv.clone(), nq, nkv, D, cos, sin, S)
+    assert _rel(got, expect) < 5e-3
+    back = native.rope_qkv_(got.clone(), nq, nkv, D, cos, sin, S, inverse=True)
+    assert _rel(back, qkv) < 1e-2
+    assert torch.equal(got[:, (nq + nkv) * D:], qkv[:, (nq + nkv) * D:])  # v untouched
+
+
+def test_swiglu():
+    T, I = 300, 688
+    gu = torch.randn(T, 2 * I, device="cuda").bfloat16()
+    a = native.swiglu_gu_fwd(gu)
+    assert _rel(a, ref.swiglu_gu_fwd(gu.float())) < 5e-3
+    da = torch.randn(T, I, device="cuda").bfloat16()
+    dgu = native.swiglu_gu_bwd(da, gu)
+    assert _rel(dgu, ref.swiglu_gu_bwd(da.float(), gu.float())) < 5e-3
+
+
+def test_embedding():
+    V, H, T = 1000, 256, 777
+    w = torch.randn(V, H, device="cuda").bfloat16()
+    ids = torch.randint(0, 50, (T,), device="cuda")  # many repeats
+    h = native.embedding_fwd(ids, w)
+    assert torch.equal(h, w[ids])
+    dh = torch.randn(T, H, device="cuda").bfloat16()
+    dw = native.embedding_bwd(dh, ids, V)
+    dwe = ref.embedding_bwd(dh.float(), ids, V)
+    assert _rel(dw, dwe) < 5e-3
+    dw2 = native.embedding_bwd(dh, ids, V)
+    assert torch.equal(dw, dw2)  # deterministic
+
+
+@pytest.mark.parametrize("T,V", [(64, 1024), (513, 128256)])
+def test_cross_entropy(T, V):
+    logits = (torch.randn(T, V, device="cuda") * 2).bfloat16()
+    tgt = torch.randint(0, V, (T,), device="cuda")
+    tgt[::7] = -100
+    loss_e, g_e, n = ref.cross_entropy_fwd_bwd(logits.float(), tgt)
+    work = logits.clone()
+    loss, g, cnt = native.cross_entropy_fwd_bwd(work, tgt)
+    assert int(cnt.item()) == n
+    assert math.isclose(loss.item(), loss_e.item(), rel_tol=1e-4)
+    assert _rel(g, g_e) < 1e-2
