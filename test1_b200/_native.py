@@ -36,12 +36,26 @@ def host():
     mod = _load("_host")
     if not getattr(host, "_configured", False):
         n = int(os.environ.get("T1_HOST_THREADS", "0") or 0)
-        cpus = _cpu_list_from_env()
+        cpus = _cpu_list_from_env() or _rank_cpu_slice()
         if n <= 0:
             n = len(cpus) if cpus else len(os.sched_getaffinity(0))
         mod.configure_threads(n, cpus)
         host._configured = True
     return mod
+
+
+def _rank_cpu_slice() -> list[int]:
+    """Without an explicit CPU list, local ranks split the process affinity
+    mask evenly (contiguous blocks), so N ranks on one host do not run N
+    full-size worker pools on the same cores."""
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", "1") or 1)
+    if local_world <= 1:
+        return []
+    local_rank = int(os.environ.get("LOCAL_RANK", "0") or 0)
+    cpus = sorted(os.sched_getaffinity(0))
+    per = max(1, len(cpus) // local_world)
+    part = cpus[local_rank * per:(local_rank + 1) * per]
+    return part or cpus[-per:]
 
 
 def cuda():

@@ -120,6 +120,9 @@ static void adam_kernel(const AdamArgs& a, int64_t begin, int64_t end) {
   const R eps = V::set1(h.eps), bc2 = V::set1(h.bc2_rsqrt);
   const R step = V::set1(h.step_size), wd = V::set1(h.wd), wdstep = V::set1(h.wd_step);
   const R gscale = V::set1(h.grad_scale);
+  // The shadow is write-only: stream it past the caches when its vectors
+  // are aligned (saves the read-for-ownership of every shadow line).
+  const bool nt = HDT >= 0 && V::template can_stream<(HDT < 0 ? kBF16 : HDT)>(sh + begin);
 
   auto body = [&](int64_t j) __attribute__((always_inline)) {
     R gr = g ? V::mul(V::template ld<GDT>(g + j), gscale) : V::zero();
@@ -140,7 +143,10 @@ static void adam_kernel(const AdamArgs& a, int64_t begin, int64_t end) {
     V::template st<PDT>(p + j, pr);
     V::template st<SDT>(m + j, mr);
     V::template st<SDT>(v + j, vr);
-    if (HDT >= 0) V::template st<(HDT < 0 ? kBF16 : HDT)>(sh + j, pr);
+    if (HDT >= 0) {
+      if (nt) V::template st_stream<(HDT < 0 ? kBF16 : HDT)>(sh + j, pr);
+      else V::template st<(HDT < 0 ? kBF16 : HDT)>(sh + j, pr);
+    }
   };
 
   int64_t i = begin;
@@ -173,6 +179,7 @@ static void adam_kernel(const AdamArgs& a, int64_t begin, int64_t end) {
     Elem<SDT>::st(v + i, vv);
     if (HDT >= 0) Elem<(HDT < 0 ? kBF16 : HDT)>::st(sh + i, pv);
   }
+  if (nt) V::fence();
 }
 
 template <int PDT, int GDT, int SDT>

@@ -31,6 +31,12 @@ struct V {
   }
   template <int DT, class T> static inline R ld(const T* p);
   template <int DT, class T> static inline void st(T* p, R x);
+  template <int DT, class T> static inline void st_stream(T* p, R x);
+  // streaming stores need the vector's natural alignment
+  template <int DT, class T> static inline bool can_stream(const T* p) {
+    return (reinterpret_cast<uintptr_t>(p) % (sizeof(T) * W)) == 0;
+  }
+  static inline void fence() { _mm_sfence(); }
 };
 
 template <> inline __m256 V::ld<kF32, float>(const float* p) { return _mm256_loadu_ps(p); }
@@ -55,6 +61,20 @@ template <> inline void V::st<kBF16, uint16_t>(uint16_t* p, __m256 x) {
 template <> inline void V::st<kF16, uint16_t>(uint16_t* p, __m256 x) {
   _mm_storeu_si128(reinterpret_cast<__m128i*>(p), _mm256_cvtps_ph(x, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC));
 }
+template <> inline void V::st_stream<kBF16, uint16_t>(uint16_t* p, __m256 x) {
+  __m256i u = _mm256_castps_si256(x);
+  __m256i lsb = _mm256_and_si256(_mm256_srli_epi32(u, 16), _mm256_set1_epi32(1));
+  __m256i r = _mm256_srli_epi32(_mm256_add_epi32(u, _mm256_add_epi32(lsb, _mm256_set1_epi32(0x7fff))), 16);
+  __m256 nan = _mm256_cmp_ps(x, x, _CMP_UNORD_Q);
+  r = _mm256_castps_si256(_mm256_blendv_ps(_mm256_castsi256_ps(r),
+                                           _mm256_castsi256_ps(_mm256_set1_epi32(0x7fc0)), nan));
+  __m128i packed = _mm_packus_epi32(_mm256_castsi256_si128(r), _mm256_extracti128_si256(r, 1));
+  _mm_stream_si128(reinterpret_cast<__m128i*>(p), packed);
+}
+template <> inline void V::st_stream<kF16, uint16_t>(uint16_t* p, __m256 x) {
+  _mm_stream_si128(reinterpret_cast<__m128i*>(p), _mm256_cvtps_ph(x, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC));
+}
+template <> inline void V::st_stream<kF32, float>(float* p, __m256 x) { _mm256_stream_ps(p, x); }
 }  // namespace avx2
 }  // namespace t1h
 

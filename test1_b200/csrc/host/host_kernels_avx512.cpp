@@ -24,6 +24,12 @@ struct V {
   static inline double hsum(R a) { return _mm512_reduce_add_ps(a); }
   template <int DT, class T> static inline R ld(const T* p);
   template <int DT, class T> static inline void st(T* p, R x);
+  template <int DT, class T> static inline void st_stream(T* p, R x);
+  // streaming stores need the vector's natural alignment
+  template <int DT, class T> static inline bool can_stream(const T* p) {
+    return (reinterpret_cast<uintptr_t>(p) % (sizeof(T) * W)) == 0;
+  }
+  static inline void fence() { _mm_sfence(); }
 };
 
 template <> inline __m512 V::ld<kF32, float>(const float* p) { return _mm512_loadu_ps(p); }
@@ -46,6 +52,18 @@ template <> inline void V::st<kBF16, uint16_t>(uint16_t* p, __m512 x) {
 template <> inline void V::st<kF16, uint16_t>(uint16_t* p, __m512 x) {
   _mm256_storeu_si256(reinterpret_cast<__m256i*>(p), _mm512_cvtps_ph(x, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC));
 }
+template <> inline void V::st_stream<kBF16, uint16_t>(uint16_t* p, __m512 x) {
+  __m512i u = _mm512_castps_si512(x);
+  __m512i lsb = _mm512_and_si512(_mm512_srli_epi32(u, 16), _mm512_set1_epi32(1));
+  __m512i r = _mm512_srli_epi32(_mm512_add_epi32(u, _mm512_add_epi32(lsb, _mm512_set1_epi32(0x7fff))), 16);
+  __mmask16 nan = _mm512_cmp_ps_mask(x, x, _CMP_UNORD_Q);
+  r = _mm512_mask_mov_epi32(r, nan, _mm512_set1_epi32(0x7fc0));
+  _mm256_stream_si256(reinterpret_cast<__m256i*>(p), _mm512_cvtepi32_epi16(r));
+}
+template <> inline void V::st_stream<kF16, uint16_t>(uint16_t* p, __m512 x) {
+  _mm256_stream_si256(reinterpret_cast<__m256i*>(p), _mm512_cvtps_ph(x, _MM_FROUND_TO_NEAREST_INT | _MM_FROUND_NO_EXC));
+}
+template <> inline void V::st_stream<kF32, float>(float* p, __m512 x) { _mm512_stream_ps(p, x); }
 }  // namespace avx512
 }  // namespace t1h
 

@@ -21,6 +21,9 @@ struct V {
   static inline double hsum(R a) { return a; }
   template <int DT, class T> static inline R ld(const T* p);
   template <int DT, class T> static inline void st(T* p, R x);
+  template <int DT, class T> static inline bool can_stream(const T*) { return false; }
+  template <int DT, class T> static inline void st_stream(T* p, R x) { st<DT>(p, x); }
+  static inline void fence() {}
 };
 }  // namespace scalar
 }  // namespace t1h

@@ -76,9 +76,13 @@ class CommStrategy:
             return (0, numel) if self.rank == 0 else (0, 0)
         return shard_bounds(numel, self.world, self.rank)
 
-    @property
-    def updaters(self) -> int:
-        return 1 if (self.world == 1 or self.rank0_optimizer) else self.world
+    def updaters_for(self, numel: int) -> int:
+        """How many ranks publish an update of a layer of ``numel`` elements
+        (ranks whose update range is empty do not)."""
+        if self.world == 1 or self.rank0_optimizer:
+            return 1
+        ss = shard_size(numel, self.world)
+        return max(1, -(-numel // ss))
 
     @property
     def grad_scale(self) -> float:
@@ -153,7 +157,7 @@ class CollectiveComm(CommStrategy):
         with stream.ctx():
             if self.grad_mode == "cpu_reduce":
                 slot = self.cpu_slots.acquire_for_write(st.idx)
-                slot.copy_(src[:P], non_blocking=True)
+                slot[:P].copy_(src[:P], non_blocking=True)
                 return
             if self.rank0_optimizer:
                 dist.reduce(src[:P], dst=0, group=self.grad_group)
@@ -248,7 +252,7 @@ class CpuReduceSlots:
         s, e = rng
         out = None
         if e > s:
-            srcs = [self._slot(layer, r)[s:e] for r in range(self.world)]
+            srcs = [self._slot(layer, r)[s:e] for r in range(self.world)]  # slots hold [0, P)
             out = st.grad_host
             self._host.sum_slots_(out, srcs, 1.0)
         self._host.counter_add(self.counters, self._consumed(layer), 1)

@@ -171,8 +171,9 @@ class SlideFSDP(nn.Module):
         self._n_slots = 4
         self._slots_off = None
         if self.world_size > 1 and config.grad_sync_mode == "cpu_reduce":
+            es = torch.tensor([], dtype=self.dtype).element_size()
             self._slots_off = plan.take(CpuReduceSlots.region_bytes(self._slot_cap, self.world_size,
-                                                                    self._n_slots))
+                                                                    self._n_slots, es))
         shm_path = None
         if self.world_size > 1:
             shm_path = f"/dev/shm/t1b200_{self._session}.bin"
@@ -190,7 +191,8 @@ class SlideFSDP(nn.Module):
         if self._slots_off is not None:
             slot_region = _SubRegion(self.shared, self._slots_off)
             cpu_slots = CpuReduceSlots(slot_region, self.counters, 2 * self.num_layers, self.num_layers,
-                                       self._slot_cap, self.rank, self.world_size, self._n_slots)
+                                       self._slot_cap, self.rank, self.world_size, self._n_slots,
+                                       dtype=self.dtype)
         self.cpu_slots = cpu_slots
         self.comm = make_comm(config, self.device, self.rank, self.world_size, cpu_slots)
 
@@ -347,8 +349,8 @@ class SlideFSDP(nn.Module):
         return sum(max(0, st.shard[1] - st.shard[0]) for st in self.layer_states)
 
     # ------------------------------------------------------ layer movement
-    def _update_target(self) -> int:
-        return self.comm.updaters * self.completed_steps
+    def _update_target(self, st: LayerRuntimeState) -> int:
+        return self.comm.updaters_for(st.numel) * self.completed_steps
 
     def _fetch(self, st: LayerRuntimeState, with_grad: bool, need_weights: bool = True) -> None:
         """Acquire a pool unit for ``st`` and enqueue its parameter load."""
@@ -360,7 +362,7 @@ class SlideFSDP(nn.Module):
         st.unit = unit
         if need_weights:
             # the previous step's optimizer update of this layer must be visible
-            self.updates.wait_counter(st.idx, self._update_target())
+            self.updates.wait_counter(st.idx, self._update_target(st))
             self.h2d_stream.wait(unit.free_event)
             self.comm.fetch_params(st, unit.param, self.h2d_stream)
             self.h2d_bytes += st.numel * unit.param.element_size()
@@ -401,7 +403,8 @@ class SlideFSDP(nn.Module):
             if has_work:
                 g = grad if grad is not None else st.grad_host
                 opt.step_flat(st.idx, g, shadow=shadow, grad_scale=scale)
-            self.updates.publish(st.idx)
+            if e > s:  # only ranks that own a slice publish
+                self.updates.publish(st.idx)
 
         if self._reducer is not None:
             def run_reduce():
@@ -542,7 +545,7 @@ class SlideFSDP(nn.Module):
             self._reducer.drain()
         self.updates.drain()
         for st in self.layer_states:
-            self.updates.wait_counter(st.idx, self._update_target())
+            self.updates.wait_counter(st.idx, self._update_target(st))
 
     def update_learning_rate(self, new_lr: float) -> None:
         self.wait_for_updates()
@@ -564,7 +567,7 @@ class SlideFSDP(nn.Module):
             if st.grad_host is not None and st.grad_host.numel():
                 sq += host.sumsq(st.grad_host) * scale2
         t = torch.tensor([sq], dtype=torch.float64, device=self.device)
-        if self.world_size > 1 and self.comm.updaters > 1:
+        if self.world_size > 1 and not self.comm.rank0_optimizer:
             dist.all_reduce(t)
         total = math.sqrt(float(t.item()))
         coef = max_norm / (total + 1e-6)

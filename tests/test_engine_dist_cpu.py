@@ -1,0 +1,77 @@
+"""Multi-rank engine on CPU/gloo (2 ranks) vs a single-process oracle:
+HF LlamaForCausalLM whose per-step gradient is the mean of the ranks'
+per-rank mean-loss gradients, stepped by torch.optim.AdamW."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tests._dist_worker import batches, run_engine
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _oracle(world, steps):
+    import transformers
+
+    from test1_b200.models.llama import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig.tiny()
+    torch.manual_seed(0)
+    ours = LlamaForCausalLM(cfg)
+    hf = transformers.LlamaForCausalLM(cfg.to_hf()).float()
+    hf.config._attn_implementation = "eager"
+    hf.load_state_dict({n: p.detach().clone() for n, p in ours.named_parameters()})
+    opt = torch.optim.AdamW(hf.parameters(), lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
+    losses = []
+    for step_batches in batches(cfg, world, steps):
+        opt.zero_grad()
+        per_rank = []
+        for ids in step_batches:
+            loss = hf(input_ids=ids, labels=ids).loss / world
+            loss.backward()
+            per_rank.append(float(loss) * world)
+        opt.step()
+        losses.append(per_rank)
+    return losses, dict(hf.named_parameters())
+
+
+@pytest.mark.parametrize("mode,grad,sharding,ckpt", [
+    ("full", "cpu_reduce", "rank", True),
+    ("full", "gpu_reduce", "rank", True),
+    ("shard", "gpu_reduce", "rank", False),
+    ("shard", "cpu_reduce", "rank", True),
+    ("full", "gpu_reduce", "rank0", True),
+])
+def test_two_rank_engine_matches_oracle(tmp_path, mode, grad, sharding, ckpt):
+    world, steps = 2, 3
+    out = str(tmp_path / "res.pt")
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=run_engine, args=(r, world, port, mode, grad, sharding, steps, out, ckpt))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    errs = [f for f in os.listdir(tmp_path) if ".err" in f]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    assert all(p.exitcode == 0 for p in procs)
+    res0 = torch.load(out)
+    res1 = torch.load(out + ".1")
+    oracle_losses, oracle_params = _oracle(world, steps)
+    for s in range(steps):
+        assert abs(res0["losses"][s] - oracle_losses[s][0]) < 1e-4
+        assert abs(res1["losses"][s] - oracle_losses[s][1]) < 1e-4
+    for n, p in oracle_params.items():
+        d = (res0["master"][n].view(p.shape) - p.detach()).abs()
+        assert (d > 1e-4).float().mean().item() < 1e-3, n
+        assert d.max().item() < 3 * 2 * 1e-3, n

@@ -141,3 +141,22 @@ def test_cross_entropy(T, V):
     assert int(cnt.item()) == n
     assert math.isclose(loss.item(), loss_e.item(), rel_tol=1e-4)
     assert _rel(g, g_e) < 1e-2
+
+
+@pytest.mark.parametrize("B,S,nq,nkv", [(2, 128, 4, 2), (1, 1024, 32, 8), (2, 256, 8, 8)])
+def test_attention_fwd_bwd(B, S, nq, nkv):
+    D = 128
+    T = B * S
+    g = torch.Generator(device="cuda").manual_seed(S + nq)
+    qkv = torch.randn(T, (nq + 2 * nkv) * D, device="cuda", generator=g).bfloat16()
+    o, lse = native.attention_qkv_fwd(qkv, nq, nkv, D, S)
+    oe, lsee = ref.attention_qkv_fwd(qkv.float(), nq, nkv, D, S)
+    assert _rel(o, oe) < 1e-2
+    assert torch.allclose(lse, lsee, atol=2e-3, rtol=1e-3)
+    do = torch.randn(T, nq * D, device="cuda", generator=g).bfloat16()
+    dqkv = native.attention_qkv_bwd(do, qkv, o, lse, nq, nkv, D, S)
+    dqkve = ref.attention_qkv_bwd(do.float(), qkv.float(), o.float(), lse, nq, nkv, D, S)
+    nqd, nkd = nq * D, nkv * D
+    assert _rel(dqkv[:, :nqd], dqkve[:, :nqd]) < 2e-2, "dq"
+    assert _rel(dqkv[:, nqd:nqd + nkd], dqkve[:, nqd:nqd + nkd]) < 2e-2, "dk"
+    assert _rel(dqkv[:, nqd + nkd:], dqkve[:, nqd + nkd:]) < 2e-2, "dv"
