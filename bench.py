@@ -239,6 +239,16 @@ def run_reference(args, rank, world, local):
 
 def main():
     args = parse_args()
+    if args.impl == "reference":
+        # OpenMP reads its thread count when torch loads: set it first, the
+        # way the reference's numa_launch.sh does for each rank.
+        from baseline.reference_arm import omp_threads_for_rank
+
+        n = omp_threads_for_rank(int(os.environ.get("LOCAL_RANK", "0")),
+                                 int(os.environ.get("LOCAL_WORLD_SIZE", "1")),
+                                 len(os.sched_getaffinity(0)))
+        os.environ["OMP_NUM_THREADS"] = str(n)
+        os.environ["MKL_NUM_THREADS"] = str(n)
     rank, world, local = init_dist(args)
     import torch
 
@@ -280,7 +290,8 @@ def main():
     }
     if args.impl == "reference":
         line["impl"] = "reference"
-    extra = {k: res[k] for k in ("init_s", "h2d_gb_per_step", "adam_busy_s_per_step", "losses") if k in res}
+    extra = {k: res[k] for k in ("init_s", "h2d_gb_per_step", "adam_busy_s_per_step", "losses",
+                                 "attn_implementation") if k in res}
     line["detail"] = extra
     if rank == 0:
         print(json.dumps(line), flush=True)
