@@ -1,0 +1,26 @@
+"""One GEMM shape, a few launches: the small case for an ncu capture of the
+tcgen05 GEMM (Llama-3.1-8B QKV projection: 4096 x 6144 x 4096, ~130 MB of
+operands).  Usage: python benchmark/gemm_profile_case.py [fwd|dgrad|wgrad]"""
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+from test1_b200.ops import native  # noqa: E402
+
+kind = sys.argv[1] if len(sys.argv) > 1 else "fwd"
+M, N, K = 4096, 6144, 4096
+x = torch.randn(M, K, device="cuda").bfloat16()
+w = torch.randn(N, K, device="cuda").bfloat16()
+dy = torch.randn(M, N, device="cuda").bfloat16()
+for _ in range(3):
+    if kind == "fwd":
+        native.gemm(x, w, torch.empty(M, N, device="cuda", dtype=torch.bfloat16))
+    elif kind == "dgrad":
+        native.gemm(dy, w, torch.empty(M, K, device="cuda", dtype=torch.bfloat16), False, True)
+    else:
+        native.gemm(dy, x, torch.empty(N, K, device="cuda", dtype=torch.bfloat16), True, True)
+torch.cuda.synchronize()
+assert native.gemm_error() == 0
+print("ok", kind)

@@ -26,6 +26,7 @@ struct AdamHyper {
   float grad_scale;  // multiplies every gradient element before use
   int adamw;         // 1: decoupled decay (AdamW), 0: L2 added to the gradient
   int has_wd;        // wd > 0
+  int stream_shadow; // 1: non-temporal stores for the shadow when aligned
 };
 
 struct AdamArgs {

@@ -122,7 +122,8 @@ static void adam_kernel(const AdamArgs& a, int64_t begin, int64_t end) {
   const R gscale = V::set1(h.grad_scale);
   // The shadow is write-only: stream it past the caches when its vectors
   // are aligned (saves the read-for-ownership of every shadow line).
-  const bool nt = HDT >= 0 && V::template can_stream<(HDT < 0 ? kBF16 : HDT)>(sh + begin);
+  const bool nt = HDT >= 0 && h.stream_shadow &&
+                  V::template can_stream<(HDT < 0 ? kBF16 : HDT)>(sh + begin);
 
   auto body = [&](int64_t j) __attribute__((always_inline)) {
     R gr = g ? V::mul(V::template ld<GDT>(g + j), gscale) : V::zero();

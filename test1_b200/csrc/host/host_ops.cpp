@@ -13,6 +13,7 @@
 #include <unistd.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <cmath>
 #include <cstring>
 #include <memory>
@@ -146,6 +147,11 @@ AdamHyper make_hyper(int64_t step, double lr, double beta1, double beta2, double
   h.grad_scale = static_cast<float>(grad_scale);
   h.adamw = adamw ? 1 : 0;
   h.has_wd = wd > 0 ? 1 : 0;
+  static const int stream_shadow = [] {
+    const char* e = std::getenv("T1_STREAM_SHADOW");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  h.stream_shadow = stream_shadow;
   return h;
 }
 

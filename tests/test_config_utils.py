@@ -1,0 +1,118 @@
+"""Config validation/round trip, shard math, datasets, FLOPs metric, NUMA
+placement on a fake sysfs, split-plane relayout."""
+import json
+import os
+
+import pytest
+import torch
+
+from test1_b200 import SlideFSDPConfig
+from test1_b200.runtime.layer_state import shard_bounds, shard_size
+from test1_b200.runtime.numa import parse_cpulist, plan
+from test1_b200.utils.datasets import DummyDataset, UniformTokens
+from test1_b200.utils.metric import calculate_flops_per_batch
+from test1_b200.utils.param_reuse import fp32_to_split_planes_, split_planes_to_fp32_
+
+
+def test_config_defaults_and_validation():
+    c = SlideFSDPConfig(device="cpu")
+    assert c.param_transfer_mode == "full" and c.grad_sync_mode == "gpu_reduce"
+    assert c.gpu_buffer_pool_size == 2 and c.adam_betas == (0.9, 0.999)
+    with pytest.raises(ValueError, match="param_transfer_mode must be 'full' or 'shard'"):
+        SlideFSDPConfig(device="cpu", param_transfer_mode="x")
+    with pytest.raises(ValueError, match="grad_sync_mode must be"):
+        SlideFSDPConfig(device="cpu", grad_sync_mode="x")
+    with pytest.raises(ValueError, match="ac_offload_mode must be"):
+        SlideFSDPConfig(device="cpu", ac_offload_mode="disk")
+    with pytest.raises(ValueError):
+        SlideFSDPConfig(device="cpu", dtype=torch.int8)
+
+
+def test_config_device_from_local_rank(monkeypatch):
+    monkeypatch.setenv("LOCAL_RANK", "3")
+    assert SlideFSDPConfig().device == torch.device("cuda", 3)
+
+
+def test_config_dict_round_trip():
+    c = SlideFSDPConfig.from_dict({"dtype": "fp16", "device": "cpu", "adam_betas": [0.8, 0.9],
+                                   "param_transfer_mode": "shard", "unknown_key": 1})
+    assert c.dtype == torch.float16 and c.adam_betas == (0.8, 0.9) and c.param_transfer_mode == "shard"
+    d = c.to_dict()
+    assert d["dtype"] == "float16" and d["device"] == "cpu"
+    c2 = SlideFSDPConfig.from_dict(json.loads(json.dumps(d)))
+    assert c2.to_dict() == d
+
+
+@pytest.mark.parametrize("P,N", [(1, 2), (100, 3), (218112000, 8), (64 * 7 + 5, 4), (10, 8)])
+def test_shard_bounds_cover_exactly(P, N):
+    covered = []
+    for r in range(N):
+        s, e = shard_bounds(P, N, r)
+        assert (s % 64 == 0 or s == P) and e <= P and s <= e
+        covered.extend(range(s, e)) if P < 10000 else covered.append((s, e))
+    if P < 10000:
+        assert covered == list(range(P))
+    assert shard_size(P, N) * N >= P
+
+
+def test_dummy_dataset_semantics():
+    ds = DummyDataset(size=8, max_length=128, vocab_size=500)
+    for i in range(8):
+        s = ds[i]
+        ids, mask, labels = s["input_ids"], s["attention_mask"], s["labels"]
+        assert ids.min() >= 1 and ids.max() < 500
+        n = int(mask.sum())
+        assert 128 // 3 <= n < 127
+        assert not mask[n:].any() and mask[:n].all()
+        assert (labels[~mask] == -100).all()
+        assert (labels[:10] == -100).all()
+        assert torch.equal(labels[100:n], ids[100:n]) or n <= 100
+    u = UniformTokens(4, 64, 1000)[0]
+    assert torch.equal(u["labels"], u["input_ids"]) and u["attention_mask"].all()
+
+
+def test_flops_metric_llama8b():
+    from test1_b200.models.llama import LlamaConfig
+
+    f = calculate_flops_per_batch(LlamaConfig.llama31_8b(), 4, 1024)
+    # ~6 * P_nonembed * T + attention + vocab terms for 4096 tokens
+    assert 1.8e14 < f < 2.2e14
+    assert calculate_flops_per_batch(LlamaConfig.llama31_8b(), 4, 1024, with_recompute=True) > f
+
+
+def test_numa_plan_fake_sysfs(tmp_path):
+    root = tmp_path
+    for n, cpus in [(0, "0-7"), (1, "8-15")]:
+        d = root / f"sys/devices/system/node/node{n}"
+        d.mkdir(parents=True)
+        (d / "cpulist").write_text(cpus)
+    for c in range(16):
+        d = root / f"sys/devices/system/cpu/cpu{c}/topology"
+        d.mkdir(parents=True)
+        (d / "thread_siblings_list").write_text(str(c))
+    buses = ["00000000:11:00.0", "00000000:12:00.0", "00000000:91:00.0", "00000000:92:00.0"]
+    for b, node in zip(buses, [0, 0, 1, 1]):
+        d = root / f"sys/bus/pci/devices/{b[4:].lower()}"
+        d.mkdir(parents=True)
+        (d / "numa_node").write_text(str(node))
+    allowed = list(range(16))
+    p0 = plan(0, 4, 0, allowed, 1, str(root), buses)
+    p1 = plan(1, 4, 1, allowed, 1, str(root), buses)
+    p2 = plan(2, 4, 2, allowed, 1, str(root), buses)
+    assert p0["NUMA_NODE"] == "0" and p2["NUMA_NODE"] == "1"
+    assert parse_cpulist(p0["NUMA_CONTROL_CORES"]) == [0]
+    assert parse_cpulist(p0["NUMA_CPU_ADAM_CORES"]) == [1, 2, 3]
+    assert parse_cpulist(p1["NUMA_CPU_ADAM_CORES"]) == [5, 6, 7]
+    assert parse_cpulist(p2["NUMA_CONTROL_CORES"]) == [8]
+    a = set(parse_cpulist(p0["NUMA_CPU_ADAM_CORES"])) | set(parse_cpulist(p0["NUMA_CONTROL_CORES"]))
+    b = set(parse_cpulist(p1["NUMA_CPU_ADAM_CORES"])) | set(parse_cpulist(p1["NUMA_CONTROL_CORES"]))
+    assert not (a & b)
+
+
+def test_split_planes_round_trip():
+    x = torch.randn(1000) * 10
+    orig = x.clone()
+    bf = fp32_to_split_planes_(x)
+    assert (bf.float() - orig).abs().max() <= orig.abs().max() * 2 ** -8
+    split_planes_to_fp32_(x)
+    assert torch.equal(x, orig)
