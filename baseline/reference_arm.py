@@ -79,6 +79,11 @@ def build_hf_model(model_name: str, device_for_init):
     with torch.device("meta"):
         model = LlamaForCausalLM(hf_cfg)
     model = model.to_empty(device="cpu").to(torch.bfloat16)
+    # to_empty leaves non-persistent buffers (the rotary inv_freq) unset:
+    # rebuild the rotary module from the config
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+
+    model.model.rotary_emb = LlamaRotaryEmbedding(config=hf_cfg)
     gen = torch.Generator(device=device_for_init).manual_seed(42)
     with torch.no_grad():
         for name, p in model.named_parameters():
@@ -133,7 +138,7 @@ def run(args, rank, world, local):
     losses = []
     for i in range(args.warmup):
         out = engine(input_ids=dev_batches[i], labels=dev_batches[i])
-        losses.append(float(out.loss))
+        losses.append(float(out.loss.detach()))
     drain()
     barrier()
 
@@ -155,7 +160,7 @@ def run(args, rank, world, local):
     barrier()
     clocks = sampler.stop()
     dev_ms = max_over_ranks(start.elapsed_time(end), world)
-    losses.append(float(last))
+    losses.append(float(last.detach()))
 
     e2e = None
     if not args.no_e2e:
