@@ -180,6 +180,7 @@ def run_ours(args, rank, world, local):
     launches0 = native_launch_count()
     h2d0 = engine.h2d_bytes
     adam0 = engine.updates.busy_s
+    blocked0 = engine.updates.blocked_s
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     barrier(world)
@@ -199,6 +200,7 @@ def run_ours(args, rank, world, local):
     losses.append(float(last))
     h2d_per_step = (engine.h2d_bytes - h2d0) / args.steps
     adam_busy = (engine.updates.busy_s - adam0) / args.steps
+    blocked = (engine.updates.blocked_s - blocked0) / args.steps
 
     # ---- end-to-end loop through the public API: pinned host batch copied
     # in every step, loss read back every step
@@ -228,6 +230,7 @@ def run_ours(args, rank, world, local):
     return {
         "dev_ms": dev_ms, "e2e": e2e, "clocks": clocks, "launches": launches, "init_s": init_s,
         "losses": losses, "h2d_gb_per_step": h2d_per_step / 1e9, "adam_busy_s_per_step": adam_busy,
+        "fetch_blocked_on_adam_s_per_step": blocked, "comm": engine.comm.name,
     }
 
 
@@ -290,7 +293,8 @@ def main():
     }
     if args.impl == "reference":
         line["impl"] = "reference"
-    extra = {k: res[k] for k in ("init_s", "h2d_gb_per_step", "adam_busy_s_per_step", "losses",
+    extra = {k: res[k] for k in ("init_s", "h2d_gb_per_step", "adam_busy_s_per_step",
+                                 "fetch_blocked_on_adam_s_per_step", "comm", "losses",
                                  "attn_implementation") if k in res}
     line["detail"] = extra
     if rank == 0:

@@ -11,6 +11,8 @@ Extra fields (all optional, reference configs never set them):
         default) or "rank0" (the reference's single-optimizer placement).
     fused_comm: use the fused NVLink kernels for shard all-gather and
         gpu_reduce reduce-scatter when available (else NCCL).
+    shard_source: what shard mode reads from host memory: the fp32
+        "master" (cast to bf16 on the GPU) or the bf16 "shadow".
     host_threads: size of the per-rank host worker pool (0 = all CPUs in the
         affinity mask).
     use_native_kernels: run the model on the sm_100a kernels (True) or on
@@ -74,6 +76,7 @@ class SlideFSDPConfig:
     # ---- fields without a reference counterpart --------------------------
     optimizer_sharding: str = "rank"
     fused_comm: bool = True
+    shard_source: str = "master"  # shard fetch reads the fp32 "master" (cast on GPU) or the bf16 "shadow"
     host_threads: int = 0
     use_native_kernels: Optional[bool] = None  # None: native iff device is CUDA
 
@@ -101,6 +104,8 @@ class SlideFSDPConfig:
             raise ValueError(
                 f"optimizer_sharding must be 'rank' or 'rank0', got {self.optimizer_sharding}"
             )
+        if self.shard_source not in ("master", "shadow"):
+            raise ValueError(f"shard_source must be 'master' or 'shadow', got {self.shard_source}")
         if self.gpu_buffer_pool_size < 2:
             raise ValueError("gpu_buffer_pool_size must be >= 2 (current layer + prefetched layer)")
         if not 0.0 <= self.optimizer_nvme_offload_fraction <= 1.0:

@@ -27,6 +27,15 @@ std::vector<torch::Tensor> attention_fwd(torch::Tensor qkv, int64_t n_q, int64_t
                                          int64_t S);
 torch::Tensor attention_bwd(torch::Tensor dout, torch::Tensor qkv, torch::Tensor out,
                             torch::Tensor lse, int64_t n_q, int64_t n_kv, int64_t D, int64_t S);
+void fused_rs_d2h(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t world,
+                  int64_t offset, int64_t n, torch::Tensor host_out, double scale, int64_t epoch,
+                  torch::Tensor counter, torch::Tensor err);
+void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t world,
+                        int64_t offset, int64_t n, torch::Tensor host_src, int64_t epoch,
+                        torch::Tensor counter, torch::Tensor err);
+void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Tensor out,
+                  torch::Tensor ptrs, torch::Tensor sigs, torch::Tensor shards, int64_t rank,
+                  int64_t world, torch::Tensor host_src, int64_t epoch, torch::Tensor counters);
 }  // namespace t1
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -45,4 +54,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_check_error", &t1::gemm_check_error, pybind11::arg("reset") = false);
   m.def("attention_fwd", &t1::attention_fwd);
   m.def("attention_bwd", &t1::attention_bwd);
+  m.def("fused_rs_d2h", &t1::fused_rs_d2h);
+  m.def("fused_shard_gather", &t1::fused_shard_gather);
+  m.def("fused_ag_qkv", &t1::fused_ag_qkv);
 }

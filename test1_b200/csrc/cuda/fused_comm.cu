@@ -1,0 +1,252 @@
+// Fused NVLink collectives of the sliding engine (sm_100a, one process per
+// GPU, buffers in symmetric memory mapped into every peer).
+//
+//  * fused_rs_d2h: the gpu_reduce path.  Rank r reads its shard
+//    [offset, offset + n) of the layer gradient from every peer's pool unit
+//    (P2P loads over NVLink), sums in fp32, multiplies by `scale` (1/N),
+//    rounds to bf16 and stores straight into its page-locked host gradient
+//    shard (zero-copy, mapped memory).  One kernel replaces NCCL
+//    reduce_scatter + a device-to-host copy.
+//
+//  * fused_shard_gather: the shard path.  Rank r reads its shard of the
+//    layer's master from page-locked host memory (fp32 master, cast to bf16
+//    here, or the bf16 shadow), and stores it into every peer's pool unit at
+//    the shard offset (P2P stores over NVLink).  One kernel replaces a
+//    host-to-device copy + NCCL all_gather (+ the cast).
+//
+// Cross-GPU ordering uses per-buffer signal pads (uint32 slots in each
+// rank's pad, written by peers with release stores at system scope, read
+// with acquire loads).  Slot layout: [0, W) "ready/free" from peer p,
+// [W, 2W) "done" from peer p.  Values are monotonically increasing epochs
+// (one per launch on that buffer, identical on all ranks), so pads never
+// need resetting.  Every wait is bounded (%globaltimer, 4 s); on expiry the
+// kernel writes an error code and returns without touching more data.
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace t1 {
+namespace fused {
+
+using bf16 = __nv_bfloat16;
+constexpr int kMaxRanks = 8;
+
+struct Peers {
+  uint64_t ptr[kMaxRanks];  // base address of the symmetric buffer on each rank
+  uint64_t sig[kMaxRanks];  // signal pad base on each rank
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until pad[slot0 + p] >= epoch for every p < world.  Thread-local.
+__device__ __forceinline__ bool wait_all(const uint32_t* pad, int slot0, int world, uint32_t epoch) {
+  const uint64_t t0 = sm100::globaltimer_ns();
+  for (int p = 0; p < world; ++p) {
+    uint32_t n = 0;
+    while (ld_acquire_sys(pad + slot0 + p) < epoch) {
+      if ((++n & 255u) == 0 && sm100::globaltimer_ns() - t0 > sm100::kWaitLimitNs) return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void signal_all(const Peers& pe, int slot, int world, uint32_t epoch) {
+  for (int p = 0; p < world; ++p)
+    st_release_sys(reinterpret_cast<uint32_t*>(pe.sig[p]) + slot, epoch);
+}
+
+// Block-wide "all peers reached slot0 phase" barrier entry; returns false
+// (for every thread) when the wait expired.
+__device__ __forceinline__ bool block_wait(const uint32_t* my_pad, int slot0, int world,
+                                           uint32_t epoch, int* err, int code) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = wait_all(my_pad, slot0, world, epoch) ? 1 : 0;
+    if (!ok && err) atomicCAS(err, 0, code);
+    __threadfence_system();
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// The last CTA to finish signals `slot` (done) to every peer and waits for
+// theirs; `counter` is a device-local int reset by that CTA.
+__device__ __forceinline__ void finish(const Peers& pe, int rank, int world, uint32_t epoch,
+                                       int* counter, int* err, int code) {
+  __threadfence_system();  // every thread's peer / host stores are visible system-wide
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(counter, 1);
+    if (prev == static_cast<int>(gridDim.x) - 1) {
+      signal_all(pe, world + rank, world, epoch);
+      const uint32_t* my_pad = reinterpret_cast<const uint32_t*>(pe.sig[rank]);
+      if (!wait_all(my_pad, world, world, epoch) && err) atomicCAS(err, 0, code);
+      atomicExch(counter, 0);
+    }
+  }
+}
+
+// ---------------------------------------------------------- reduce-scatter
+__global__ void __launch_bounds__(256) rs_d2h_kernel(Peers pe, int rank, int world, long offset,
+                                                     long n, bf16* __restrict__ host_out,
+                                                     float scale, uint32_t epoch, int* counter,
+                                                     int* err) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) signal_all(pe, rank, world, epoch);  // my grads ready
+  const uint32_t* my_pad = reinterpret_cast<const uint32_t*>(pe.sig[rank]);
+  if (!block_wait(my_pad, 0, world, epoch, err, 201)) return;
+  const long n8 = n >> 3;
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll 1
+    for (int p = 0; p < world; ++p) {
+      const bf16* src = reinterpret_cast<const bf16*>(pe.ptr[p]) + offset + 8 * i;
+      int4 raw = __ldcg(reinterpret_cast<const int4*>(src));
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 f = __bfloat1622float2(h[k]);
+        acc[2 * k] += f.x;
+        acc[2 * k + 1] += f.y;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] *= scale;
+    store8(host_out + 8 * i, acc);
+  }
+  // tail (n % 8) by block 0
+  if (blockIdx.x == 0) {
+    for (long j = (n8 << 3) + threadIdx.x; j < n; j += blockDim.x) {
+      float s = 0.f;
+      for (int p = 0; p < world; ++p)
+        s += __bfloat162float(reinterpret_cast<const bf16*>(pe.ptr[p])[offset + j]);
+      host_out[j] = __float2bfloat16_rn(s * scale);
+    }
+  }
+  finish(pe, rank, world, epoch, counter, err, 202);
+}
+
+// ------------------------------------------------------------ shard gather
+template <bool SRC_F32>
+__global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, int world, long offset,
+                                                           long n, const void* __restrict__ host_src,
+                                                           uint32_t epoch, int* counter, int* err) {
+  // my unit is free (stream order): announce it, wait until every peer's is
+  if (blockIdx.x == 0 && threadIdx.x == 0) signal_all(pe, rank, world, epoch);
+  const uint32_t* my_pad = reinterpret_cast<const uint32_t*>(pe.sig[rank]);
+  if (!block_wait(my_pad, 0, world, epoch, err, 211)) return;
+  const long n8 = n >> 3;
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
+    int4 out;
+    if (SRC_F32) {
+      const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(host_src) + 8 * i);
+      float4 a = s[0], b = s[1];
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
+      h[0] = __floats2bfloat162_rn(a.x, a.y);
+      h[1] = __floats2bfloat162_rn(a.z, a.w);
+      h[2] = __floats2bfloat162_rn(b.x, b.y);
+      h[3] = __floats2bfloat162_rn(b.z, b.w);
+    } else {
+      out = *reinterpret_cast<const int4*>(static_cast<const bf16*>(host_src) + 8 * i);
+    }
+#pragma unroll 1
+    for (int p = 0; p < world; ++p) {
+      bf16* dst = reinterpret_cast<bf16*>(pe.ptr[p]) + offset + 8 * i;
+      *reinterpret_cast<int4*>(dst) = out;
+    }
+  }
+  if (blockIdx.x == 0) {
+    for (long j = (n8 << 3) + threadIdx.x; j < n; j += blockDim.x) {
+      bf16 v = SRC_F32 ? __float2bfloat16_rn(static_cast<const float*>(host_src)[j])
+                       : static_cast<const bf16*>(host_src)[j];
+      for (int p = 0; p < world; ++p) reinterpret_cast<bf16*>(pe.ptr[p])[offset + j] = v;
+    }
+  }
+  finish(pe, rank, world, epoch, counter, err, 212);
+}
+
+}  // namespace fused
+
+// ================================================================ host side
+static fused::Peers make_peers(torch::Tensor ptrs, torch::Tensor sigs, int world) {
+  TORCH_CHECK(world >= 1 && world <= fused::kMaxRanks, "world size must be 1..8");
+  TORCH_CHECK(ptrs.device().is_cpu() && ptrs.scalar_type() == torch::kInt64 && ptrs.numel() == world,
+              "peer pointers must be a CPU int64 tensor of world entries");
+  TORCH_CHECK(sigs.device().is_cpu() && sigs.scalar_type() == torch::kInt64 && sigs.numel() == world,
+              "signal pads must be a CPU int64 tensor of world entries");
+  fused::Peers pe;
+  auto pa = ptrs.accessor<int64_t, 1>();
+  auto sa = sigs.accessor<int64_t, 1>();
+  for (int i = 0; i < fused::kMaxRanks; ++i) {
+    pe.ptr[i] = i < world ? static_cast<uint64_t>(pa[i]) : 0;
+    pe.sig[i] = i < world ? static_cast<uint64_t>(sa[i]) : 0;
+    if (i < world) TORCH_CHECK(pe.ptr[i] % 16 == 0, "peer buffer ", i, " is not 16-byte aligned");
+  }
+  return pe;
+}
+
+static int comm_grid(long n8) {
+  long want = (n8 + 255) / 256;
+  long cap = 2L * num_sms();
+  return static_cast<int>(std::max<long>(1, std::min(want, cap)));
+}
+
+void fused_rs_d2h(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t world,
+                  int64_t offset, int64_t n, torch::Tensor host_out, double scale, int64_t epoch,
+                  torch::Tensor counter, torch::Tensor err) {
+  auto pe = make_peers(ptrs, sigs, world);
+  TORCH_CHECK(host_out.scalar_type() == torch::kBFloat16 && host_out.is_contiguous() &&
+                  host_out.numel() >= n, "host_out must be a contiguous bf16 tensor of >= n elements");
+  TORCH_CHECK(offset % 8 == 0, "shard offset must be a multiple of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(host_out.data_ptr()) % 16 == 0, "host_out misaligned");
+  TORCH_CHECK(counter.is_cuda() && err.is_cuda(), "counter/err must live on the GPU");
+  if (n <= 0) return;
+  void* out_dev = host_out.data_ptr();
+  if (host_out.device().is_cpu()) {
+    T1_CHECK_CUDA(cudaHostGetDevicePointer(&out_dev, host_out.data_ptr(), 0));
+  }
+  fused::rs_d2h_kernel<<<comm_grid(n / 8), 256, 0, stream()>>>(
+      pe, rank, world, offset, n, reinterpret_cast<__nv_bfloat16*>(out_dev), (float)scale,
+      static_cast<uint32_t>(epoch), counter.data_ptr<int>(), err.data_ptr<int>());
+  check_launch("fused_rs_d2h");
+  count_launch();
+}
+
+void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t world,
+                        int64_t offset, int64_t n, torch::Tensor host_src, int64_t epoch,
+                        torch::Tensor counter, torch::Tensor err) {
+  auto pe = make_peers(ptrs, sigs, world);
+  TORCH_CHECK(host_src.is_contiguous() && host_src.numel() >= n, "host_src too small");
+  TORCH_CHECK(host_src.scalar_type() == torch::kFloat32 || host_src.scalar_type() == torch::kBFloat16,
+              "host_src must be fp32 (master) or bf16 (shadow)");
+  TORCH_CHECK(offset % 8 == 0, "shard offset must be a multiple of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(host_src.data_ptr()) % 16 == 0, "host_src misaligned");
+  if (n <= 0) return;
+  const void* src_dev = host_src.data_ptr();
+  if (host_src.device().is_cpu()) {
+    void* d = nullptr;
+    T1_CHECK_CUDA(cudaHostGetDevicePointer(&d, host_src.data_ptr(), 0));
+    src_dev = d;
+  }
+  const int grid = comm_grid(n / 8);
+  if (host_src.scalar_type() == torch::kFloat32)
+    fused::shard_gather_kernel<true><<<grid, 256, 0, stream()>>>(
+        pe, rank, world, offset, n, src_dev, static_cast<uint32_t>(epoch), counter.data_ptr<int>(),
+        err.data_ptr<int>());
+  else
+    fused::shard_gather_kernel<false><<<grid, 256, 0, stream()>>>(
+        pe, rank, world, offset, n, src_dev, static_cast<uint32_t>(epoch), counter.data_ptr<int>(),
+        err.data_ptr<int>());
+  check_launch("fused_shard_gather");
+  count_launch();
+}
+
+}  // namespace t1

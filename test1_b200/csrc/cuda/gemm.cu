@@ -26,249 +26,10 @@
 // Tiles are visited in grouped (GROUP_M) raster order for L2 reuse.  All
 // barrier waits are bounded (see sm100.cuh); a timeout writes a code to the
 // error word and the CTA unwinds.
-#include "common.cuh"
-#include "sm100.cuh"
+#include "gemm_core.cuh"
 
 namespace t1 {
 
-using bf16 = __nv_bfloat16;
-using namespace sm100;
-
-namespace gemm {
-
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 64;
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 512;
-constexpr int GROUP_M = 16;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
-
-enum Epilogue : int { kStore = 0, kAddResidual = 1 };
-
-struct Params {
-  int M, N, K;
-  bf16* C;
-  long ldc;
-  const bf16* R;
-  long ldr;
-  int tiles_m, tiles_n, num_tiles, k_blocks;
-  int* err;
-};
-
-__device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
-  const int group = GROUP_M * tiles_n;
-  const int gid = tile / group;
-  const int first_m = gid * GROUP_M;
-  const int gsz = min(tiles_m - first_m, GROUP_M);
-  const int in_group = tile % group;
-  mb = first_m + in_group % gsz;
-  nb = in_group / gsz;
-}
-
-template <bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(192, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a,
-                     const __grid_constant__ CUtensorMap tma_b, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const ErrorSlot err{p.err};
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
-    }
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0 && lane == 0) {
-    prefetch_tensormap(&tma_a);
-    prefetch_tensormap(&tma_b);
-  }
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 0) {
-    // ------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t armed_parity[STAGES];
-      bool armed[STAGES];
-#pragma unroll
-      for (int s = 0; s < STAGES; ++s) armed[s] = false;
-      for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x) {
-        int mb, nb;
-        raster(tile, p.tiles_m, p.tiles_n, mb, nb);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1)) {
-            err.set(101);
-            *abort_flag = 1;
-            break;
-          }
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          armed[stage] = true;
-          armed_parity[stage] = phase;
-          uint8_t* a = sA + stage * A_BYTES;
-          uint8_t* b = sB + stage * B_BYTES;
-          const int k0 = kb * BK;
-          if (!A_MN) {
-            tma_load_2d(a, &tma_a, &full[stage], k0, mb * BM);
-          } else {
-            tma_load_2d(a, &tma_a, &full[stage], mb * BM, k0);
-            tma_load_2d(a + 8192, &tma_a, &full[stage], mb * BM + 64, k0);
-          }
-          if (!B_MN) {
-            tma_load_2d(b, &tma_b, &full[stage], k0, nb * BN);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(b + j * 8192, &tma_b, &full[stage], nb * BN + 64 * j, k0);
-          }
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
-      // On abort, let every load this thread issued land before the CTA
-      // exits (each wait is itself bounded).
-      if (*abort_flag) {
-        for (int s = 0; s < STAGES; ++s)
-          if (armed[s]) mbar_wait(&full[s], armed_parity[s]);
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, A_MN, B_MN);
-      int stage = 0;
-      uint32_t phase = 0;
-      int local = 0;
-      for (int tile = blockIdx.x; tile < p.num_tiles && !*abort_flag; tile += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
-          err.set(102);
-          *abort_flag = 1;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
-        bool ok = true;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase)) {
-            err.set(103);
-            *abort_flag = 1;
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
-#pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + k * 2048, 8192, 1024)
-                                     : smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + k * 2048, 8192, 1024)
-                                     : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            mma_bf16(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
-          }
-          mma_commit(&empty[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-        if (!ok) break;
-        mma_commit(&tfull[acc]);
-      }
-    }
-  } else {
-    // --------------------------------------------------------- epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    int local = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
-      if (*abort_flag) break;
-      if (!mbar_wait(&tfull[acc], acc_phase)) {
-        err.set(104);
-        *abort_flag = 1;
-        break;
-      }
-      tc_fence_after();
-      int mb, nb;
-      raster(tile, p.tiles_m, p.tiles_n, mb, nb);
-      const int row = mb * BM + q * 32 + lane;
-      const bool row_ok = row < p.M;
-      bf16* crow = p.C + static_cast<long>(row) * p.ldc;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + c, r);
-        tmem_ld_wait();
-        const int col0 = nb * BN + c;
-        if (row_ok) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int col = col0 + 8 * v;
-            if (col < p.N) {
-              float f[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);
-              if (EPI == kAddResidual) {
-                float rv[8];
-                load8(p.R + static_cast<long>(row) * p.ldr + col, rv);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) f[j] += rv[j];
-              }
-              store8(crow + col, f);
-            }
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
-  }
-}
-
-}  // namespace gemm
 
 // ================================================================ host side
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -291,7 +52,7 @@ static EncodeTiledFn encode_fn() {
 
 // 2-D bf16 tensor map, 128B swizzle: `inner` contiguous elements per row,
 // `outer` rows, `ld` elements between rows, box = 64 x box_outer.
-static CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld,
+CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld,
                             int box_outer) {
   TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "GEMM operand must be 16-byte aligned");
   TORCH_CHECK((ld * 2) % 16 == 0, "GEMM operand row stride must be a multiple of 8 elements");
@@ -323,7 +84,7 @@ torch::Tensor& gemm_error_word() {
 
 template <bool A_MN, bool B_MN, int EPI>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p) {
-  auto kern = gemm::gemm_bf16_kernel<A_MN, B_MN, EPI>;
+  auto kern = gemm::gemm_bf16_kernel<A_MN, B_MN, EPI, false>;
   static bool configured = false;
   if (!configured) {
     T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -331,7 +92,8 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p
     configured = true;
   }
   const int grid = std::min(p.num_tiles, num_sms());
-  kern<<<grid, 192, gemm::SMEM_BYTES, stream()>>>(ta, tb, p);
+  gemm::AgParams none{};
+  kern<<<grid, 192, gemm::SMEM_BYTES, stream()>>>(ta, tb, p, none);
   check_launch("gemm_bf16");
   count_launch();
 }

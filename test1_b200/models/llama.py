@@ -252,12 +252,18 @@ class LlamaDecoderLayer(nn.Module):
         return g_qkv, gs[3], g_gu, gs[6], gs[7], gs[8]
 
     # forward ---------------------------------------------------------------
-    def forward_train(self, h: torch.Tensor, ctx: StepContext, save: bool = True):
+    def forward_train(self, h: torch.Tensor, ctx: StepContext, save: bool = True, qkv_fn=None):
+        """``qkv_fn(x1)``, when given, produces the QKV projection (the engine
+        passes the fused all-gather + QKV GEMM of shard mode); the other
+        weights are read after it returns."""
         cfg = self.cfg
         Hq, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
-        w_qkv, w_o, w_gu, w_down = self._w()
         x1, rstd1 = ops.rmsnorm_fwd(h, self.input_layernorm.weight.data, cfg.rms_norm_eps)
-        qkv = ops.linear_fwd(x1, w_qkv)
+        if qkv_fn is not None:
+            qkv = qkv_fn(x1)
+        else:
+            qkv = ops.linear_fwd(x1, self._w()[0])
+        w_qkv, w_o, w_gu, w_down = self._w()
         ops.rope_qkv_(qkv, Hq, Hkv, D, ctx.cos, ctx.sin, ctx.seq_len)
         o, lse = ops.attention_fwd(qkv, Hq, Hkv, D, ctx.seq_len)
         h2 = ops.linear_fwd(o, w_o, residual=h)

@@ -110,6 +110,13 @@ class CommStrategy:
     def barrier(self) -> None:
         pass
 
+    def allocator(self, dtype: torch.dtype):
+        """Allocation function for pool buffers (None: plain device memory)."""
+        return None
+
+    def check(self) -> None:
+        """Raise if an asynchronous communication kernel reported an error."""
+
     def close(self) -> None:
         pass
 
@@ -262,4 +269,9 @@ class CpuReduceSlots:
 def make_comm(config, device: torch.device, rank: int, world: int, cpu_slots=None) -> CommStrategy:
     if world == 1:
         return CommStrategy(config, device, 0, 1)
+    if getattr(config, "fused_comm", False):
+        from .fused import FusedComm, symmetric_memory_available
+
+        if symmetric_memory_available(device, world):
+            return FusedComm(config, device, rank, world, cpu_slots)
     return CollectiveComm(config, device, rank, world, cpu_slots)

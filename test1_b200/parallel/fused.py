@@ -1,0 +1,165 @@
+"""Fused NVLink communication for the sliding engine (one process per GPU,
+all GPUs of one node).
+
+The pool units live in symmetric memory (``torch.distributed._symmetric_memory``:
+one allocation per buffer, mapped into every rank, plus a per-buffer signal
+pad).  Two sm_100a kernels (``csrc/cuda/fused_comm.cu``) replace NCCL on the
+engine's hot paths:
+
+  gpu_reduce   ``fused_rs_d2h``: reduce-scatter of the layer gradient over
+               NVLink (P2P loads from every peer's unit), scaled by 1/N,
+               rounded to bf16 and stored directly into this rank's
+               page-locked host gradient shard (zero-copy).
+  shard        ``fused_shard_gather``: this rank's shard of the layer master
+               is read from page-locked host memory (fp32, cast on the GPU),
+               and stored into every peer's unit (P2P stores over NVLink).
+
+Buffers keep a per-buffer epoch counter (identical on every rank because the
+schedule is); kernels signal and wait on it with bounded waits and report
+expiry through an error word that ``check()`` turns into an exception.
+cpu_reduce keeps the shared-memory slot reduction of ``CollectiveComm``.
+"""
+from __future__ import annotations
+
+from typing import Dict, Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import _native
+from ..runtime.device import Stream
+from ..runtime.layer_state import LayerRuntimeState, shard_bounds
+from .comm import CollectiveComm
+
+
+def symmetric_memory_available(device: torch.device, world: int) -> bool:
+    if device.type != "cuda" or world < 2 or world > 8:
+        return False
+    try:
+        import torch.distributed._symmetric_memory  # noqa: F401
+    except Exception:
+        return False
+    return True
+
+
+class SymmetricBuffer:
+    """A symmetric allocation plus what the kernels need: peer base
+    pointers, peer signal pads, an epoch counter and a completion counter."""
+
+    def __init__(self, numel: int, dtype: torch.dtype, device: torch.device, group):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.tensor = symm_mem.empty(numel, dtype=dtype, device=device)
+        self.handle = symm_mem.rendezvous(self.tensor, group)
+        self.ptrs = torch.tensor(list(self.handle.buffer_ptrs), dtype=torch.int64)
+        self.sigs = torch.tensor(list(self.handle.signal_pad_ptrs), dtype=torch.int64)
+        self.epoch = 0
+        self.counter = torch.zeros(1, dtype=torch.int32, device=device)
+        self.ag_counters = torch.zeros(65, dtype=torch.int32, device=device)
+        world = len(self.handle.buffer_ptrs)
+        need = (2 * world + 64 * world) * 4
+        if self.handle.signal_pad_size < need:
+            raise RuntimeError(f"symmetric-memory signal pad of {self.handle.signal_pad_size} bytes is "
+                               f"smaller than the {need} bytes the fused kernels use")
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch
+
+
+class FusedComm(CollectiveComm):
+    name = "fused-nvlink"
+
+    def __init__(self, config, device: torch.device, rank: int, world: int, cpu_slots=None):
+        super().__init__(config, device, rank, world, cpu_slots)
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = dist.group.WORLD
+        try:
+            symm_mem.enable_symm_mem_for_group(self.group.group_name)
+        except Exception:
+            pass
+        self._bufs: Dict[int, SymmetricBuffer] = {}
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.fused_grads = self.grad_mode == "gpu_reduce" and not self.rank0_optimizer
+        self.fused_params = self.param_mode == "shard"
+        src = getattr(config, "shard_source", "master")
+        self.shard_source = src if src in ("master", "shadow") else "master"
+
+    # pool allocation -----------------------------------------------------
+    def unit_capacity(self, numel: int) -> int:
+        if self.fused_grads or self.fused_params:
+            return numel
+        return super().unit_capacity(numel)
+
+    def allocator(self, dtype: torch.dtype):
+        def alloc(n: int) -> torch.Tensor:
+            b = SymmetricBuffer(n, dtype, self.device, self.group)
+            self._bufs[b.tensor.data_ptr()] = b
+            return b.tensor
+        return alloc
+
+    def _buf(self, t: torch.Tensor) -> SymmetricBuffer:
+        b = self._bufs.get(t.data_ptr())
+        if b is None:
+            raise RuntimeError("fused communication needs pool units allocated in symmetric memory")
+        return b
+
+    @property
+    def grad_scale(self) -> float:
+        # the fused reduce-scatter already multiplies by 1/N
+        return 1.0 if self.fused_grads else 1.0 / self.world
+
+    # operations ----------------------------------------------------------
+    def fetch_params(self, st: LayerRuntimeState, dst: torch.Tensor, stream: Stream) -> None:
+        if not self.fused_params:
+            return super().fetch_params(st, dst, stream)
+        s, e = shard_bounds(st.numel, self.world, self.rank)
+        b = self._buf(dst)
+        src = st.master[s:e] if self.shard_source == "master" else st.shadow[s:e]
+        with stream.ctx():
+            _native.cuda().fused_shard_gather(b.ptrs, b.sigs, self.rank, self.world, s, e - s,
+                                              src, b.next_epoch(), b.counter, self.err)
+
+    def sync_grads(self, st: LayerRuntimeState, src: torch.Tensor, stream: Stream) -> None:
+        if not self.fused_grads:
+            return super().sync_grads(st, src, stream)
+        s, e = shard_bounds(st.numel, self.world, self.rank)
+        b = self._buf(src)
+        out = st.grad_host if st.grad_host is not None else torch.empty(0, dtype=src.dtype)
+        with stream.ctx():
+            _native.cuda().fused_rs_d2h(b.ptrs, b.sigs, self.rank, self.world, s, e - s, out,
+                                        1.0 / self.world, b.next_epoch(), b.counter, self.err)
+
+    # shard-mode forward: layer fetch fused with the QKV projection -----
+    def can_fuse_qkv(self, st: LayerRuntimeState) -> bool:
+        return self.fused_params and st.kind == "decoder" and self.device.type == "cuda"
+
+    def shard_table(self, numel: int) -> torch.Tensor:
+        key = numel
+        t = self._shard_tables.get(key) if hasattr(self, "_shard_tables") else None
+        if t is None:
+            if not hasattr(self, "_shard_tables"):
+                self._shard_tables = {}
+            t = torch.tensor([list(shard_bounds(numel, self.world, q)) for q in range(self.world)],
+                             dtype=torch.int64)
+            self._shard_tables[key] = t
+        return t
+
+    def ag_qkv(self, st: LayerRuntimeState, x1: torch.Tensor, n_rows: int) -> torch.Tensor:
+        """Gather layer ``st`` into every rank's unit and return x1 @ W_qkv^T
+        (one kernel, on the current stream)."""
+        s, e = shard_bounds(st.numel, self.world, self.rank)
+        b = self._buf(st.unit.param)
+        src = st.master[s:e] if self.shard_source == "master" else st.shadow[s:e]
+        out = torch.empty(x1.shape[0], n_rows, dtype=x1.dtype, device=x1.device)
+        _native.cuda().fused_ag_qkv(x1, b.tensor, n_rows, out, b.ptrs, b.sigs,
+                                    self.shard_table(st.numel), self.rank, self.world, src,
+                                    b.next_epoch(), b.ag_counters)
+        return out
+
+    def check(self) -> None:
+        code = int(self.err.item())
+        if code:
+            raise RuntimeError(f"fused NVLink kernel reported error {code} (a bounded cross-GPU wait "
+                               f"expired: a peer rank stalled or died)")

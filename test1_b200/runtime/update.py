@@ -55,6 +55,7 @@ class UpdateScheduler:
         self._error: Optional[BaseException] = None
         self._stop = False
         self.busy_s = 0.0
+        self.blocked_s = 0.0  # time callers spent in wait_counter
         self._thread = threading.Thread(target=self._loop, name=name, daemon=True)
         self._thread.start()
 
@@ -74,17 +75,23 @@ class UpdateScheduler:
 
     def wait_counter(self, layer: int, target: int, timeout_s: Optional[float] = None) -> None:
         """Block until counter[layer] >= target (all updaters finished)."""
+        if self._host.counter_load(self.counters, layer) >= target:
+            return
         timeout = self.timeout_s if timeout_s is None else timeout_s
-        deadline = time.monotonic() + timeout
-        while True:
-            self.raise_if_failed()
-            remaining = deadline - time.monotonic()
-            if remaining <= 0:
-                raise TimeoutError(
-                    f"layer {layer} parameter update timed out: counter "
-                    f"{self.counter(layer)} < {target} after {timeout:.1f}s (a peer rank may have died)")
-            if self._host.counter_wait_geq(self.counters, layer, target, min(remaining, 0.5)):
-                return
+        t0 = time.monotonic()
+        deadline = t0 + timeout
+        try:
+            while True:
+                self.raise_if_failed()
+                remaining = deadline - time.monotonic()
+                if remaining <= 0:
+                    raise TimeoutError(
+                        f"layer {layer} parameter update timed out: counter "
+                        f"{self.counter(layer)} < {target} after {timeout:.1f}s (a peer rank may have died)")
+                if self._host.counter_wait_geq(self.counters, layer, target, min(remaining, 0.5)):
+                    return
+        finally:
+            self.blocked_s += time.monotonic() - t0
 
     def drain(self, timeout_s: Optional[float] = None) -> None:
         timeout = self.timeout_s if timeout_s is None else timeout_s

@@ -230,10 +230,13 @@ class SlideFSDP(nn.Module):
         self.layer_optimizer = self._create_optimizer(config)
 
         # ---- GPU buffer pools
+        alloc = self.comm.allocator(self.dtype)
         self.pool = LayerBufferPool(max(self.comm.unit_capacity(c) for c in dec_caps) if dec_caps else 1,
-                                    self.dtype, self.device, config.gpu_buffer_pool_size, name="decoder-pool")
+                                    self.dtype, self.device, config.gpu_buffer_pool_size,
+                                    allocator=alloc, name="decoder-pool")
         self.big_pool = LayerBufferPool(max(self.comm.unit_capacity(c) for c in big_caps),
-                                        self.dtype, self.device, 1, name="embed/output-unit")
+                                        self.dtype, self.device, 1, allocator=alloc,
+                                        name="embed/output-unit")
         for st in self.layer_states:
             st.pool = self.pool if st.kind == "decoder" else self.big_pool
 
@@ -371,6 +374,19 @@ class SlideFSDP(nn.Module):
             st.loaded = unit.free_event
         st.bind_device(with_grad=with_grad)
 
+    def _acquire_unloaded(self, st: LayerRuntimeState) -> None:
+        """Take a pool unit for ``st`` whose weights a fused kernel on the
+        compute stream will load; the compute stream waits until the unit's
+        previous occupant is done with it."""
+        self.updates.wait_counter(st.idx, self._update_target(st))
+        unit = st.pool.acquire(st.idx)
+        st.unit = unit
+        if unit.free_event is not None and unit.free_event.e is not None:
+            torch.cuda.current_stream(self.device).wait_event(unit.free_event.e)
+        st.loaded = None
+        st.bind_device(with_grad=False)
+        self.h2d_bytes += st.numel * unit.param.element_size()
+
     def _wait_loaded(self, st: LayerRuntimeState) -> None:
         if st.loaded is not None and st.loaded.e is not None:
             torch.cuda.current_stream(self.device).wait_event(st.loaded.e)
@@ -449,30 +465,46 @@ class SlideFSDP(nn.Module):
 
         # ---------------- forward
         self._fetch(emb, with_grad=False)
-        if L > 0:
+        fuse_first = (L > 0 and hasattr(self.comm, "can_fuse_qkv") and self.comm.can_fuse_qkv(S[1])
+                      and self.config.use_native_kernels)
+        if L > 0 and not fuse_first:
             self._fetch(S[1], with_grad=False)
         self._wait_loaded(emb)
         h = emb.module.forward_ids(ctx.input_ids)
         self._release(emb, Event(dev).record())
         prefetch = max(1, min(self.config.prefetch_layers, self.config.gpu_buffer_pool_size - 1))
+        fuse_qkv = (L > 0 and hasattr(self.comm, "can_fuse_qkv") and self.comm.can_fuse_qkv(S[1])
+                    and self.config.use_native_kernels)
+        cfgm = self.model_config
+        n_qkv = cfgm.q_size + 2 * cfgm.kv_size
         saved_all = {}
         for i in range(1, L + 1):
             st = S[i]
-            self._wait_loaded(st)
+            qkv_fn = None
+            if fuse_qkv:
+                # shard mode: the layer is gathered by its own fused QKV kernel
+                if not st.resident:
+                    self._acquire_unloaded(st)
+                    qkv_fn = (lambda x1, st=st: self.comm.ag_qkv(st, x1, n_qkv))
+                else:
+                    self._wait_loaded(st)
+            else:
+                self._wait_loaded(st)
             if self.config.enable_activation_checkpoint:
                 self.acts.save(i, h, keep_on_gpu=(i == L))
-                h, _ = st.module.forward_train(h, ctx, save=False)
+                h, _ = st.module.forward_train(h, ctx, save=False, qkv_fn=qkv_fn)
             else:
-                h, saved_all[i] = st.module.forward_train(h, ctx, save=True)
-            # prefetch the next layer(s) into free units
-            for j in range(i + 1, min(i + prefetch, L) + 1):
-                if not S[j].resident and S[j].pool.num_free:
-                    self._fetch(S[j], with_grad=False)
+                h, saved_all[i] = st.module.forward_train(h, ctx, save=True, qkv_fn=qkv_fn)
+            if not fuse_qkv:
+                # prefetch the next layer(s) into free units
+                for j in range(i + 1, min(i + prefetch, L) + 1):
+                    if not S[j].resident and S[j].pool.num_free:
+                        self._fetch(S[j], with_grad=False)
             if i == L:
                 self._fetch(out, with_grad=True)
             else:
                 self._release(st, Event(dev).record())
-            if i + 1 <= L and not S[i + 1].resident:
+            if not fuse_qkv and i + 1 <= L and not S[i + 1].resident:
                 self._fetch(S[i + 1], with_grad=False)
         if L == 0:
             self._fetch(out, with_grad=True)
@@ -541,6 +573,7 @@ class SlideFSDP(nn.Module):
     # ------------------------------------------------------------ control
     def wait_for_updates(self) -> None:
         """Block until every scheduled optimizer update (all ranks) landed."""
+        self.comm.check()
         if self._reducer is not None:
             self._reducer.drain()
         self.updates.drain()
@@ -663,6 +696,7 @@ class SlideFSDP(nn.Module):
     # --------------------------------------------------------------- misc
     def step_stats(self) -> Dict[str, float]:
         return {"h2d_bytes": float(self.h2d_bytes), "adam_busy_s": self.updates.busy_s,
+                "fetch_blocked_s": self.updates.blocked_s,
                 "ac_d2h_bytes": float(self.acts.bytes_d2h), "ac_h2d_bytes": float(self.acts.bytes_h2d)}
 
     def close(self) -> None:

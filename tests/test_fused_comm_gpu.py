@@ -1,0 +1,77 @@
+"""Fused NVLink kernels (2 GPUs): reduce-scatter + scale + zero-copy D2H and
+the shard gather from host fp32 master, against NCCL / exact expectations;
+and the engine with fused communication against the NCCL engine."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _need2():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+
+
+def _run(target, args, tmp_path, world=2):
+    ctx = mp.get_context("spawn")
+    ps = [ctx.Process(target=target, args=(r, world, *args)) for r in range(world)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=600)
+    errs = [f for f in os.listdir(tmp_path) if ".err" in f]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
+
+
+def test_fused_kernels_two_gpus(tmp_path):
+    _need2()
+    from tests._fused_worker import kernels
+
+    out = str(tmp_path / "k")
+    _run(kernels, (_port(), out), tmp_path)
+    for r in range(2):
+        res = torch.load(out + f".{r}")
+        assert res["ok"], res["msgs"]
+
+
+@pytest.mark.parametrize("mode", ["full", "shard"])
+def test_engine_fused_matches_nccl(tmp_path, mode):
+    _need2()
+    from tests._fused_worker import engine
+
+    a = str(tmp_path / "fused")
+    b = str(tmp_path / "nccl")
+    _run(engine, (_port(), a, mode, True), tmp_path)
+    _run(engine, (_port(), b, mode, False), tmp_path)
+    fa, fb = torch.load(a + ".0"), torch.load(b + ".0")
+    assert fa["comm"] == "fused-nvlink" and fb["comm"] == "collective"
+    for x, y in zip(fa["losses"], fb["losses"]):
+        assert abs(x - y) < 2e-2 * abs(y)
+    for n, t in fb["master"].items():
+        d = (fa["master"][n] - t).abs()
+        assert d.max().item() < 3 * 2 * 1e-3, n
+
+
+@pytest.mark.parametrize("src_kind", ["fp32", "bf16"])
+def test_fused_ag_qkv_two_gpus(tmp_path, src_kind):
+    _need2()
+    from tests._fused_worker import ag_gemm
+
+    out = str(tmp_path / "ag")
+    _run(ag_gemm, (_port(), out, src_kind), tmp_path)
+    for r in range(2):
+        res = torch.load(out + f".{r}")
+        assert res["ok"], res["msgs"]
