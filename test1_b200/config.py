@@ -15,6 +15,8 @@ Extra fields (all optional, reference configs never set them):
         "master" (cast to bf16 on the GPU) or the bf16 "shadow".
     host_threads: size of the per-rank host worker pool (0 = all CPUs in the
         affinity mask).
+    host_wait_timeout_s: bound on every host-side wait for another rank
+        (optimizer publication, cpu_reduce slots); expiry raises TimeoutError.
     use_native_kernels: run the model on the sm_100a kernels (True) or on
         plain PyTorch ops (False; the CPU test path).
 """
@@ -78,6 +80,7 @@ class SlideFSDPConfig:
     fused_comm: bool = True
     shard_source: str = "master"  # shard fetch reads the fp32 "master" (cast on GPU) or the bf16 "shadow"
     host_threads: int = 0
+    host_wait_timeout_s: float = 600.0  # bound on every host wait for a peer rank
     use_native_kernels: Optional[bool] = None  # None: native iff device is CUDA
 
     def __post_init__(self):

@@ -192,7 +192,7 @@ class SlideFSDP(nn.Module):
             slot_region = _SubRegion(self.shared, self._slots_off)
             cpu_slots = CpuReduceSlots(slot_region, self.counters, 2 * self.num_layers, self.num_layers,
                                        self._slot_cap, self.rank, self.world_size, self._n_slots,
-                                       dtype=self.dtype)
+                                       timeout_s=config.host_wait_timeout_s, dtype=self.dtype)
         self.cpu_slots = cpu_slots
         self.comm = make_comm(config, self.device, self.rank, self.world_size, cpu_slots)
 
@@ -244,8 +244,9 @@ class SlideFSDP(nn.Module):
         self.h2d_stream = Stream(self.device)
         self.grad_stream = Stream(self.device)
         self.ac_d2h = Stream(self.device)
-        self.updates = UpdateScheduler(self.counters)
-        self._reducer = (UpdateScheduler(self.counters, name="t1-reduce", fifo=True)
+        self.updates = UpdateScheduler(self.counters, timeout_s=config.host_wait_timeout_s)
+        self._reducer = (UpdateScheduler(self.counters, name="t1-reduce", fifo=True,
+                                         timeout_s=config.host_wait_timeout_s)
                          if cpu_slots is not None else None)
         self.acts = ActivationStore(config.ac_offload_mode if config.enable_activation_checkpoint else "gpu",
                                     self.device, self.ac_d2h, self.h2d_stream, config.ac_offload_dir)

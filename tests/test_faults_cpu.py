@@ -1,0 +1,55 @@
+"""Failure detection without any GPU fault: a rank leaves between steps and
+the surviving rank stops with a bounded, named error instead of hanging."""
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tests._fault_worker import run
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("grad_mode", ["gpu_reduce", "cpu_reduce"])
+def test_dead_rank_detected_by_survivor(tmp_path, grad_mode):
+    out = str(tmp_path / "res")
+    ctx = mp.get_context("spawn")
+    port = _port()
+    ps = [ctx.Process(target=run, args=(r, 2, port, out, grad_mode)) for r in range(2)]
+    t0 = time.time()
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=240)
+    assert time.time() - t0 < 240, "survivor hung"
+    r0 = torch.load(out + ".0")
+    r1 = torch.load(out + ".1")
+    assert r1.get("left")
+    assert r0["error"] is not None, "rank 0 should have failed"
+    msg = r0["error"].lower()
+    assert ("timed out" in msg or "timeout" in msg or "connection" in msg or "closed" in msg
+            or "peer" in msg or "gloo" in msg), r0["error"]
+
+
+def test_update_wait_timeout_names_layer():
+    from test1_b200.runtime.host_memory import HostRegion
+    from test1_b200.runtime.update import UpdateScheduler
+
+    region = HostRegion(4096)
+    ctr = region.view(torch.uint8, 0, 64)
+    sch = UpdateScheduler(ctr, timeout_s=0.3)
+    t0 = time.time()
+    with pytest.raises(TimeoutError, match="layer 3 parameter update timed out"):
+        sch.wait_counter(3, 5)
+    assert time.time() - t0 < 5
+    sch.close()
+    region.close()

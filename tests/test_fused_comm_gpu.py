@@ -60,9 +60,14 @@ def test_engine_fused_matches_nccl(tmp_path, mode):
     assert fa["comm"] == "fused-nvlink" and fb["comm"] == "collective"
     for x, y in zip(fa["losses"], fb["losses"]):
         assert abs(x - y) < 2e-2 * abs(y)
+    steps, lr = 3, 1e-3
     for n, t in fb["master"].items():
         d = (fa["master"][n] - t).abs()
-        assert d.max().item() < 3 * 2 * 1e-3, n
+        # the fused path sums in fp32 and rounds once, NCCL reduces in bf16:
+        # gradients agree to bf16 rounding; Adam turns a near-zero gradient's
+        # rounding noise into up to +-lr per step on a few elements
+        assert d.max().item() <= 2 * lr * steps + 1e-4, n
+        assert (d > 1e-3).float().mean().item() < 0.01, n
 
 
 @pytest.mark.parametrize("src_kind", ["fp32", "bf16"])
