@@ -15,6 +15,12 @@ Extra fields (all optional, reference configs never set them):
         "master" (cast to bf16 on the GPU) or the bf16 "shadow".
     host_threads: size of the per-rank host worker pool (0 = all CPUs in the
         affinity mask).
+    master_layout: how the fp32 master is stored in host memory: "split"
+        keeps each value as a bf16 high plane plus a 16-bit low plane (bit
+        exact; the high plane doubles as the bf16 copy the GPUs load, so the
+        optimizer writes no separate shadow: 2 fewer bytes of host memory
+        traffic per parameter and step), "fp32" keeps plain fp32 plus a bf16
+        shadow.  Only bf16 training uses "split".
     host_wait_timeout_s: bound on every host-side wait for another rank
         (optimizer publication, cpu_reduce slots); expiry raises TimeoutError.
     use_native_kernels: run the model on the sm_100a kernels (True) or on
@@ -81,6 +87,7 @@ class SlideFSDPConfig:
     shard_source: str = "master"  # shard fetch reads the fp32 "master" (cast on GPU) or the bf16 "shadow"
     host_threads: int = 0
     host_wait_timeout_s: float = 600.0  # bound on every host wait for a peer rank
+    master_layout: str = "split"  # "split" (hi/lo 16-bit planes) or "fp32" (plain fp32 + bf16 shadow)
     use_native_kernels: Optional[bool] = None  # None: native iff device is CUDA
 
     def __post_init__(self):
@@ -107,6 +114,8 @@ class SlideFSDPConfig:
             raise ValueError(
                 f"optimizer_sharding must be 'rank' or 'rank0', got {self.optimizer_sharding}"
             )
+        if self.master_layout not in ("split", "fp32"):
+            raise ValueError(f"master_layout must be 'split' or 'fp32', got {self.master_layout}")
         if self.shard_source not in ("master", "shadow"):
             raise ValueError(f"shard_source must be 'master' or 'shadow', got {self.shard_source}")
         if self.gpu_buffer_pool_size < 2:

@@ -11,7 +11,13 @@
 
 namespace t1h {
 
-enum HostDType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
+enum HostDType : int { kF32 = 0, kBF16 = 1, kF16 = 2, kSplit = 3 };
+
+// kSplit: an fp32 value stored as two 16-bit planes.  With b = bits(x) +
+// 0x8000 (mod 2^32), hi = b >> 16 and lo = b & 0xffff; hi alone is x rounded
+// to bf16 (nearest, ties away from zero), and ((hi << 16) | lo) - 0x8000
+// restores x exactly.  A master kept this way carries its own bf16 copy, so
+// the optimizer writes no separate shadow.
 
 struct AdamHyper {
   float beta1;
@@ -30,7 +36,8 @@ struct AdamHyper {
 };
 
 struct AdamArgs {
-  void* param;
+  void* param;       // kSplit: the hi plane
+  void* param_lo;    // kSplit only: the lo plane
   int param_dt;
   const void* grad;  // may be null: the gradient is treated as all zeros
   int grad_dt;
@@ -50,7 +57,11 @@ struct AdamArgs {
   void sum_slots_range_##ISA(const void* const* srcs, int nsrc, int src_dt,    \
                              void* dst, int dst_dt, float scale,               \
                              int64_t begin, int64_t end);                      \
-  double sumsq_range_##ISA(const void* src, int dt, int64_t begin, int64_t end);
+  double sumsq_range_##ISA(const void* src, int dt, int64_t begin, int64_t end);             \
+  void split_range_##ISA(const float* src, uint16_t* hi, uint16_t* lo, int64_t begin,        \
+                         int64_t end);                                                       \
+  void unsplit_range_##ISA(const uint16_t* hi, const uint16_t* lo, float* dst, int64_t begin, \
+                           int64_t end);
 
 T1H_DECLARE_ISA(scalar)
 T1H_DECLARE_ISA(avx2)

@@ -96,16 +96,53 @@ template <> struct Elem<kF16> {
   static inline void st(uint16_t* p, float x) { *p = s_f32_to_f16(x); }
 };
 
+// ------------------------------------------------------------- split planes
+static inline float s_split_ld(const uint16_t* hi, const uint16_t* lo, int64_t i) {
+  uint32_t b = ((static_cast<uint32_t>(hi[i]) << 16) | lo[i]) - 0x8000u;
+  float f;
+  memcpy(&f, &b, 4);
+  return f;
+}
+static inline void s_split_st(uint16_t* hi, uint16_t* lo, int64_t i, float x) {
+  uint32_t b;
+  memcpy(&b, &x, 4);
+  b += 0x8000u;
+  hi[i] = static_cast<uint16_t>(b >> 16);
+  lo[i] = static_cast<uint16_t>(b & 0xffffu);
+}
+
 // ------------------------------------------------------------------- adam
 constexpr int kNoShadow = -1;
 
+// The param access of the Adam kernel: a plain pointer, or two planes.
+template <int PDT>
+struct ParamIO {
+  using PT = typename Elem<PDT>::type;
+  PT* p;
+  ParamIO(const AdamArgs& a) : p(static_cast<PT*>(a.param)) {}
+  inline typename V::R vload(int64_t j) const { return V::template ld<PDT>(p + j); }
+  inline void vstore(int64_t j, typename V::R x) const { V::template st<PDT>(p + j, x); }
+  inline float sload(int64_t j) const { return Elem<PDT>::ld(p + j); }
+  inline void sstore(int64_t j, float x) const { Elem<PDT>::st(p + j, x); }
+};
+template <>
+struct ParamIO<kSplit> {
+  uint16_t* hi;
+  uint16_t* lo;
+  ParamIO(const AdamArgs& a)
+      : hi(static_cast<uint16_t*>(a.param)), lo(static_cast<uint16_t*>(a.param_lo)) {}
+  inline typename V::R vload(int64_t j) const { return V::split_ld(hi + j, lo + j); }
+  inline void vstore(int64_t j, typename V::R x) const { V::split_st(hi + j, lo + j, x); }
+  inline float sload(int64_t j) const { return s_split_ld(hi, lo, j); }
+  inline void sstore(int64_t j, float x) const { s_split_st(hi, lo, j, x); }
+};
+
 template <int PDT, int GDT, int SDT, int HDT>
 static void adam_kernel(const AdamArgs& a, int64_t begin, int64_t end) {
-  using PT = typename Elem<PDT>::type;
   using GT = typename Elem<GDT>::type;
   using ST = typename Elem<SDT>::type;
   using HT = typename Elem<(HDT < 0 ? kBF16 : HDT)>::type;
-  PT* p = static_cast<PT*>(a.param);
+  const ParamIO<PDT> p(a);
   const GT* g = static_cast<const GT*>(a.grad);
   ST* m = static_cast<ST*>(a.exp_avg);
   ST* v = static_cast<ST*>(a.exp_avg_sq);
@@ -127,7 +164,7 @@ static void adam_kernel(const AdamArgs& a, int64_t begin, int64_t end) {
 
   auto body = [&](int64_t j) __attribute__((always_inline)) {
     R gr = g ? V::mul(V::template ld<GDT>(g + j), gscale) : V::zero();
-    R pr = V::template ld<PDT>(p + j);
+    R pr = p.vload(j);
     R mr = V::template ld<SDT>(m + j);
     R vr = V::template ld<SDT>(v + j);
     if (l2) gr = V::fmadd(pr, wd, gr);
@@ -141,7 +178,7 @@ static void adam_kernel(const AdamArgs& a, int64_t begin, int64_t end) {
     R u = V::div(mr, d);
     if (decoupled) pr = V::fmadd(pr, wdstep, pr);
     pr = V::fmadd(u, step, pr);
-    V::template st<PDT>(p + j, pr);
+    p.vstore(j, pr);
     V::template st<SDT>(m + j, mr);
     V::template st<SDT>(v + j, vr);
     if (HDT >= 0) {
@@ -161,7 +198,7 @@ static void adam_kernel(const AdamArgs& a, int64_t begin, int64_t end) {
   for (; i + W <= end; i += W) body(i);
   for (; i < end; ++i) {
     float gv = g ? Elem<GDT>::ld(g + i) * h.grad_scale : 0.0f;
-    float pv = Elem<PDT>::ld(p + i);
+    float pv = p.sload(i);
     float mv = Elem<SDT>::ld(m + i);
     float vv = Elem<SDT>::ld(v + i);
     if (l2) gv = fmaf(pv, h.wd, gv);
@@ -175,7 +212,7 @@ static void adam_kernel(const AdamArgs& a, int64_t begin, int64_t end) {
     float u = mv / d;
     if (decoupled) pv = fmaf(pv, h.wd_step, pv);
     pv = fmaf(u, h.step_size, pv);
-    Elem<PDT>::st(p + i, pv);
+    p.sstore(i, pv);
     Elem<SDT>::st(m + i, mv);
     Elem<SDT>::st(v + i, vv);
     if (HDT >= 0) Elem<(HDT < 0 ? kBF16 : HDT)>::st(sh + i, pv);
@@ -301,6 +338,7 @@ static double sumsq_kernel(const void* src, int64_t b, int64_t e) {
 void T1H_CAT(adam_range, T1H_ISA)(const AdamArgs& a, int64_t begin, int64_t end) {
   using namespace T1H_ISA;
   switch (a.param_dt) {
+    case kSplit: return adam_dispatch_grad<kSplit>(a, begin, end);
     case kBF16: return adam_dispatch_grad<kBF16>(a, begin, end);
     case kF16: return adam_dispatch_grad<kF16>(a, begin, end);
     default: return adam_dispatch_grad<kF32>(a, begin, end);
@@ -325,6 +363,24 @@ void T1H_CAT(sum_slots_range, T1H_ISA)(const void* const* srcs, int nsrc, int sr
     case kF16: return sum_slots_dispatch_dst<kF16>(srcs, nsrc, dst, dst_dt, scale, begin, end);
     default: return sum_slots_dispatch_dst<kF32>(srcs, nsrc, dst, dst_dt, scale, begin, end);
   }
+}
+
+void T1H_CAT(split_range, T1H_ISA)(const float* src, uint16_t* hi, uint16_t* lo, int64_t begin,
+                                   int64_t end) {
+  using namespace T1H_ISA;
+  constexpr int W = V::W;
+  int64_t i = begin;
+  for (; i + W <= end; i += W) V::split_st(hi + i, lo + i, V::template ld<kF32>(src + i));
+  for (; i < end; ++i) s_split_st(hi, lo, i, src[i]);
+}
+
+void T1H_CAT(unsplit_range, T1H_ISA)(const uint16_t* hi, const uint16_t* lo, float* dst,
+                                     int64_t begin, int64_t end) {
+  using namespace T1H_ISA;
+  constexpr int W = V::W;
+  int64_t i = begin;
+  for (; i + W <= end; i += W) V::template st<kF32>(dst + i, V::split_ld(hi + i, lo + i));
+  for (; i < end; ++i) dst[i] = s_split_ld(hi, lo, i);
 }
 
 double T1H_CAT(sumsq_range, T1H_ISA)(const void* src, int dt, int64_t begin, int64_t end) {

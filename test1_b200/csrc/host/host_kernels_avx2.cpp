@@ -37,6 +37,20 @@ struct V {
     return (reinterpret_cast<uintptr_t>(p) % (sizeof(T) * W)) == 0;
   }
   static inline void fence() { _mm_sfence(); }
+  static inline R split_ld(const uint16_t* hi, const uint16_t* lo) {
+    __m256i h = _mm256_slli_epi32(_mm256_cvtepu16_epi32(_mm_loadu_si128(reinterpret_cast<const __m128i*>(hi))), 16);
+    __m256i l = _mm256_cvtepu16_epi32(_mm_loadu_si128(reinterpret_cast<const __m128i*>(lo)));
+    return _mm256_castsi256_ps(_mm256_sub_epi32(_mm256_or_si256(h, l), _mm256_set1_epi32(0x8000)));
+  }
+  static inline void split_st(uint16_t* hi, uint16_t* lo, R x) {
+    __m256i b = _mm256_add_epi32(_mm256_castps_si256(x), _mm256_set1_epi32(0x8000));
+    __m256i h = _mm256_srli_epi32(b, 16);
+    __m256i l = _mm256_and_si256(b, _mm256_set1_epi32(0xffff));
+    _mm_storeu_si128(reinterpret_cast<__m128i*>(hi),
+                     _mm_packus_epi32(_mm256_castsi256_si128(h), _mm256_extracti128_si256(h, 1)));
+    _mm_storeu_si128(reinterpret_cast<__m128i*>(lo),
+                     _mm_packus_epi32(_mm256_castsi256_si128(l), _mm256_extracti128_si256(l, 1)));
+  }
 };
 
 template <> inline __m256 V::ld<kF32, float>(const float* p) { return _mm256_loadu_ps(p); }

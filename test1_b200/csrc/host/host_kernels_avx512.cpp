@@ -30,6 +30,16 @@ struct V {
     return (reinterpret_cast<uintptr_t>(p) % (sizeof(T) * W)) == 0;
   }
   static inline void fence() { _mm_sfence(); }
+  static inline R split_ld(const uint16_t* hi, const uint16_t* lo) {
+    __m512i h = _mm512_slli_epi32(_mm512_cvtepu16_epi32(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(hi))), 16);
+    __m512i l = _mm512_cvtepu16_epi32(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(lo)));
+    return _mm512_castsi512_ps(_mm512_sub_epi32(_mm512_or_si512(h, l), _mm512_set1_epi32(0x8000)));
+  }
+  static inline void split_st(uint16_t* hi, uint16_t* lo, R x) {
+    __m512i b = _mm512_add_epi32(_mm512_castps_si512(x), _mm512_set1_epi32(0x8000));
+    _mm256_storeu_si256(reinterpret_cast<__m256i*>(hi), _mm512_cvtepi32_epi16(_mm512_srli_epi32(b, 16)));
+    _mm256_storeu_si256(reinterpret_cast<__m256i*>(lo), _mm512_cvtepi32_epi16(b));
+  }
 };
 
 template <> inline __m512 V::ld<kF32, float>(const float* p) { return _mm512_loadu_ps(p); }

@@ -24,6 +24,8 @@ struct V {
   template <int DT, class T> static inline bool can_stream(const T*) { return false; }
   template <int DT, class T> static inline void st_stream(T* p, R x) { st<DT>(p, x); }
   static inline void fence() {}
+  static inline R split_ld(const uint16_t* hi, const uint16_t* lo);
+  static inline void split_st(uint16_t* hi, uint16_t* lo, R x);
 };
 }  // namespace scalar
 }  // namespace t1h
@@ -34,5 +36,7 @@ namespace t1h {
 namespace scalar {
 template <int DT, class T> inline float V::ld(const T* p) { return Elem<DT>::ld(p); }
 template <int DT, class T> inline void V::st(T* p, float x) { Elem<DT>::st(p, x); }
+inline float V::split_ld(const uint16_t* hi, const uint16_t* lo) { return s_split_ld(hi, lo, 0); }
+inline void V::split_st(uint16_t* hi, uint16_t* lo, float x) { s_split_st(hi, lo, 0, x); }
 }  // namespace scalar
 }  // namespace t1h

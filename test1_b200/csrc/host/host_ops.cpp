@@ -83,6 +83,20 @@ static void sum_slots_range(const void* const* s, int n, int sdt, void* d, int d
     default: return sum_slots_range_scalar(s, n, sdt, d, ddt, sc, b, e);
   }
 }
+static void split_range(const float* s, uint16_t* hi, uint16_t* lo, int64_t b, int64_t e) {
+  switch (g_isa) {
+    case Isa::kAvx512: return split_range_avx512(s, hi, lo, b, e);
+    case Isa::kAvx2: return split_range_avx2(s, hi, lo, b, e);
+    default: return split_range_scalar(s, hi, lo, b, e);
+  }
+}
+static void unsplit_range(const uint16_t* hi, const uint16_t* lo, float* d, int64_t b, int64_t e) {
+  switch (g_isa) {
+    case Isa::kAvx512: return unsplit_range_avx512(hi, lo, d, b, e);
+    case Isa::kAvx2: return unsplit_range_avx2(hi, lo, d, b, e);
+    default: return unsplit_range_scalar(hi, lo, d, b, e);
+  }
+}
 static double sumsq_range(const void* s, int dt, int64_t b, int64_t e) {
   switch (g_isa) {
     case Isa::kAvx512: return sumsq_range_avx512(s, dt, b, e);
@@ -167,6 +181,7 @@ void adam_step(torch::Tensor param, c10::optional<torch::Tensor> grad, torch::Te
   TORCH_CHECK(exp_avg.scalar_type() == exp_avg_sq.scalar_type(), "state dtypes differ");
   AdamArgs a;
   a.param = param.data_ptr();
+  a.param_lo = nullptr;
   a.param_dt = host_dt(param);
   a.grad = nullptr;
   a.grad_dt = kF32;
@@ -191,6 +206,71 @@ void adam_step(torch::Tensor param, c10::optional<torch::Tensor> grad, torch::Te
                    grad_scale);
   pybind11::gil_scoped_release nogil;
   chunked(n, [&](int64_t b, int64_t e) { adam_range(a, b, e); });
+}
+
+// Adam on a split-plane master (hi plane = the bf16 copy, lo plane = the
+// rest of the fp32 bits); no separate shadow is written.
+void adam_step_split(torch::Tensor hi, torch::Tensor lo, c10::optional<torch::Tensor> grad,
+                     torch::Tensor exp_avg, torch::Tensor exp_avg_sq, int64_t step, double lr,
+                     double beta1, double beta2, double eps, double weight_decay,
+                     bool bias_correction, bool adamw_mode, double grad_scale) {
+  check_cpu_contig(hi, "hi");
+  check_cpu_contig(lo, "lo");
+  check_cpu_contig(exp_avg, "exp_avg");
+  check_cpu_contig(exp_avg_sq, "exp_avg_sq");
+  TORCH_CHECK(hi.element_size() == 2 && lo.element_size() == 2, "planes must be 16-bit");
+  const int64_t n = hi.numel();
+  TORCH_CHECK(lo.numel() == n && exp_avg.numel() == n && exp_avg_sq.numel() == n, "size mismatch");
+  AdamArgs a;
+  a.param = hi.data_ptr();
+  a.param_lo = lo.data_ptr();
+  a.param_dt = kSplit;
+  a.grad = nullptr;
+  a.grad_dt = kF32;
+  if (grad.has_value() && grad->defined()) {
+    check_cpu_contig(*grad, "grad");
+    TORCH_CHECK(grad->numel() == n, "grad size mismatch");
+    a.grad = grad->data_ptr();
+    a.grad_dt = host_dt(*grad);
+  }
+  a.exp_avg = exp_avg.data_ptr();
+  a.exp_avg_sq = exp_avg_sq.data_ptr();
+  a.state_dt = host_dt(exp_avg);
+  a.shadow = nullptr;
+  a.shadow_dt = kBF16;
+  a.h = make_hyper(step, lr, beta1, beta2, eps, weight_decay, bias_correction, adamw_mode,
+                   grad_scale);
+  pybind11::gil_scoped_release nogil;
+  chunked(n, [&](int64_t b, int64_t e) { adam_range(a, b, e); });
+}
+
+// fp32 <-> split planes
+void f32_to_split(torch::Tensor src, torch::Tensor hi, torch::Tensor lo) {
+  check_cpu_contig(src, "src");
+  check_cpu_contig(hi, "hi");
+  check_cpu_contig(lo, "lo");
+  TORCH_CHECK(src.scalar_type() == torch::kFloat32, "src must be fp32");
+  const int64_t n = src.numel();
+  TORCH_CHECK(hi.numel() == n && lo.numel() == n, "size mismatch");
+  const float* s = src.data_ptr<float>();
+  uint16_t* h = static_cast<uint16_t*>(hi.data_ptr());
+  uint16_t* l = static_cast<uint16_t*>(lo.data_ptr());
+  pybind11::gil_scoped_release nogil;
+  chunked(n, [&](int64_t b, int64_t e) { split_range(s, h, l, b, e); });
+}
+
+void split_to_f32(torch::Tensor hi, torch::Tensor lo, torch::Tensor dst) {
+  check_cpu_contig(dst, "dst");
+  check_cpu_contig(hi, "hi");
+  check_cpu_contig(lo, "lo");
+  TORCH_CHECK(dst.scalar_type() == torch::kFloat32, "dst must be fp32");
+  const int64_t n = dst.numel();
+  TORCH_CHECK(hi.numel() == n && lo.numel() == n, "size mismatch");
+  const uint16_t* h = static_cast<const uint16_t*>(hi.data_ptr());
+  const uint16_t* l = static_cast<const uint16_t*>(lo.data_ptr());
+  float* d = dst.data_ptr<float>();
+  pybind11::gil_scoped_release nogil;
+  chunked(n, [&](int64_t b, int64_t e) { unsplit_range(h, l, d, b, e); });
 }
 
 // ------------------------------------------------ reference-compatible API
@@ -450,6 +530,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("beta2"), pybind11::arg("eps"), pybind11::arg("weight_decay"),
         pybind11::arg("bias_correction") = true, pybind11::arg("adamw_mode") = true,
         pybind11::arg("grad_scale") = 1.0);
+  m.def("adam_step_split", &adam_step_split, pybind11::arg("hi"), pybind11::arg("lo"),
+        pybind11::arg("grad"), pybind11::arg("exp_avg"), pybind11::arg("exp_avg_sq"),
+        pybind11::arg("step"), pybind11::arg("lr"), pybind11::arg("beta1"), pybind11::arg("beta2"),
+        pybind11::arg("eps"), pybind11::arg("weight_decay"), pybind11::arg("bias_correction") = true,
+        pybind11::arg("adamw_mode") = true, pybind11::arg("grad_scale") = 1.0);
+  m.def("f32_to_split", &f32_to_split);
+  m.def("split_to_f32", &split_to_f32);
   m.def("create_adam", &create_adam);
   m.def("adam_update", &adam_update);
   m.def("destroy_adam", &destroy_adam);

@@ -31,9 +31,16 @@ void ThreadPool::configure(int n, const std::vector<int>& cpus) {
   std::lock_guard<std::mutex> job(job_mutex_);
   stop_workers();
   int extra = n > 1 ? n - 1 : 0;
+  uint64_t gen;
+  {
+    std::lock_guard<std::mutex> lk(mu_);
+    gen = generation_;
+  }
+  // Each worker starts from the generation current *now*, so a job posted
+  // before the thread gets scheduled is not missed.
   for (int i = 0; i < extra; ++i) {
     int cpu = cpus.empty() ? -1 : cpus[(i + 1) % cpus.size()];
-    workers_.emplace_back(&ThreadPool::worker_loop, this, i, cpu);
+    workers_.emplace_back(&ThreadPool::worker_loop, this, i, cpu, gen);
   }
   if (!cpus.empty()) {
     // The calling thread takes the first CPU of the list only while it runs
@@ -50,18 +57,14 @@ void ThreadPool::run_tasks() {
   }
 }
 
-void ThreadPool::worker_loop(int /*idx*/, int cpu) {
+void ThreadPool::worker_loop(int /*idx*/, int cpu, uint64_t start_generation) {
   if (cpu >= 0) {
     cpu_set_t set;
     CPU_ZERO(&set);
     CPU_SET(cpu, &set);
     pthread_setaffinity_np(pthread_self(), sizeof(set), &set);
   }
-  uint64_t seen = 0;
-  {
-    std::lock_guard<std::mutex> lk(mu_);
-    seen = generation_;
-  }
+  uint64_t seen = start_generation;
   for (;;) {
     {
       std::unique_lock<std::mutex> lk(mu_);

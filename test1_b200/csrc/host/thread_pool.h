@@ -33,7 +33,7 @@ class ThreadPool {
  private:
   ThreadPool() = default;
   void stop_workers();
-  void worker_loop(int idx, int cpu);
+  void worker_loop(int idx, int cpu, uint64_t start_generation);
   void run_tasks();
 
   std::vector<std::thread> workers_;

@@ -180,16 +180,24 @@ class LayerAdam:
         self._after_register(layer_idx)
         return layer_idx
 
-    def add_flat_layer(self, layer_idx: int, flat_param: torch.Tensor) -> int:
+    def add_flat_layer(self, layer_idx: int, flat_param) -> int:
         """Register one contiguous 1-D parameter slice (the engine path: the
-        rank's shard of the layer's shared fp32 master)."""
-        if flat_param.dim() != 1 or not flat_param.is_contiguous():
-            raise ValueError("flat_param must be a contiguous 1-D tensor")
+        rank's shard of the layer's shared fp32 master).  ``flat_param`` is an
+        fp32 tensor, or a (hi, lo) pair of 16-bit planes holding the fp32
+        values split (see csrc/host/host_kernels.h, kSplit)."""
+        planes = isinstance(flat_param, (tuple, list))
+        ts = list(flat_param) if planes else [flat_param]
+        for t in ts:
+            if t.dim() != 1 or not t.is_contiguous():
+                raise ValueError("flat_param must be contiguous 1-D tensor(s)")
+        if planes and (len(ts) != 2 or ts[0].numel() != ts[1].numel()):
+            raise ValueError("split master needs two planes of equal size")
         self._new_group(layer_idx, [])
-        sdt = self._state_dtype(flat_param.dtype)
-        self.exp_avg_flat[layer_idx] = torch.zeros(flat_param.numel(), dtype=sdt)
-        self.exp_avg_sq_flat[layer_idx] = torch.zeros(flat_param.numel(), dtype=sdt)
-        self._flat_param[layer_idx] = flat_param
+        n = ts[0].numel()
+        sdt = torch.float32 if (planes or self.fp32_optimizer_state) else ts[0].dtype
+        self.exp_avg_flat[layer_idx] = torch.zeros(n, dtype=sdt)
+        self.exp_avg_sq_flat[layer_idx] = torch.zeros(n, dtype=sdt)
+        self._flat_param[layer_idx] = tuple(ts) if planes else flat_param
         self._after_register(layer_idx)
         return layer_idx
 
@@ -335,8 +343,16 @@ class LayerAdam:
         group = self._group(layer_idx)
         self._pre_step(layer_idx)
         group["step"] += 1
-        self._kernel(group, self._flat_param[layer_idx], grad, self.exp_avg_flat[layer_idx],
-                     self.exp_avg_sq_flat[layer_idx], shadow, grad_scale)
+        param = self._flat_param[layer_idx]
+        if isinstance(param, tuple):
+            beta1, beta2 = group["betas"]
+            self._host.adam_step_split(
+                param[0], param[1], grad, self.exp_avg_flat[layer_idx], self.exp_avg_sq_flat[layer_idx],
+                group["step"], group["lr"], beta1, beta2, group["eps"], group["weight_decay"],
+                group["bias_correction"], group["adamw_mode"], grad_scale)
+        else:
+            self._kernel(group, param, grad, self.exp_avg_flat[layer_idx],
+                         self.exp_avg_sq_flat[layer_idx], shadow, grad_scale)
         self._post_step(layer_idx)
 
     def update_learning_rate(self, new_lr: float) -> None:

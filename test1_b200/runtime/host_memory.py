@@ -51,18 +51,44 @@ class HostRegion:
         self._cursor = 0
 
     # ------------------------------------------------------------ pinning
-    def pin(self) -> None:
+    PIN_CHUNK = 1 << 30
+
+    def pin(self, ranges: Optional[List[tuple]] = None) -> None:
+        """Page-lock the region (portable + mapped), one registration per
+        range.  ``ranges`` are (byte offset, size) pairs on page boundaries
+        that never share a page -- one per tensor a copy or kernel reads
+        (a layer's master, its shadow, a gradient slot), so every transfer
+        lies inside a single registration.  Without ranges the region is
+        registered in 1 GiB pieces.  (A single registration of tens of GB of
+        shared memory has been refused by the OS, cudaErrorOperatingSystem.)"""
         if self.pinned:
             return
-        # cudaHostRegisterPortable (1) | cudaHostRegisterMapped (2)
-        rc = torch.cuda.cudart().cudaHostRegister(self.buf.data_ptr(), self.nbytes, 3)
-        if int(rc) != 0:
-            raise RuntimeError(f"cudaHostRegister of {self.nbytes} bytes failed with error {int(rc)}")
+        rt = torch.cuda.cudart()
+        base = self.buf.data_ptr()
+        if ranges is None:
+            ranges = [(off, min(self.PIN_CHUNK, self.nbytes - off))
+                      for off in range(0, self.nbytes, self.PIN_CHUNK)]
+        self._pinned_chunks = []
+        for off, n in ranges:
+            if n <= 0:
+                continue
+            # cudaHostRegisterPortable (1) | cudaHostRegisterMapped (2)
+            rc = int(rt.cudaHostRegister(base + off, n, 3))
+            if rc != 0:
+                for p in self._pinned_chunks:
+                    rt.cudaHostUnregister(p)
+                self._pinned_chunks = []
+                raise RuntimeError(f"cudaHostRegister of bytes [{off}, {off + n}) of a {self.nbytes}-byte "
+                                   f"host region failed with error {rc}")
+            self._pinned_chunks.append(base + off)
         self.pinned = True
 
     def unpin(self) -> None:
         if self.pinned:
-            torch.cuda.cudart().cudaHostUnregister(self.buf.data_ptr())
+            rt = torch.cuda.cudart()
+            for p in getattr(self, "_pinned_chunks", []):
+                rt.cudaHostUnregister(p)
+            self._pinned_chunks = []
             self.pinned = False
 
     # -------------------------------------------------------------- views
@@ -102,3 +128,58 @@ class RegionPlanner:
         off = _align(self.size, self.align)
         self.size = off + nbytes
         return off
+
+
+class MasterStore:
+    """One layer's fp32 master in host memory, stored either as plain fp32
+    plus a separate bf16 shadow, or "split": a bf16 high plane (which *is*
+    the shadow) followed by a 16-bit low plane (see host_kernels.h, kSplit).
+    All fp32 reads and writes go through this class."""
+
+    def __init__(self, region: "HostRegion", numel: int, master_off: int, split: bool,
+                 shadow_dtype: torch.dtype, shadow_off: Optional[int] = None):
+        self.numel = numel
+        self.split = split
+        if split:
+            self.hi = region.view(torch.bfloat16, master_off, numel)
+            self.lo = region.view(torch.int16, master_off + 2 * numel, numel)
+            self.f32 = None
+            self.shadow = self.hi
+        else:
+            self.f32 = region.view(torch.float32, master_off, numel)
+            self.hi = self.lo = None
+            if shadow_dtype == torch.float32 or shadow_off is None:
+                self.shadow = self.f32
+            else:
+                self.shadow = region.view(shadow_dtype, shadow_off, numel)
+
+    @staticmethod
+    def bytes_needed(numel: int, split: bool, shadow: bool) -> tuple:
+        """(master bytes, shadow bytes) to plan for one layer."""
+        return 4 * numel, (0 if split or not shadow else 2 * numel)
+
+    @property
+    def bind_tensor(self) -> torch.Tensor:
+        """Flat tensor the offloaded module parameters point into."""
+        return self.hi if self.split else self.f32
+
+    def read_fp32(self, s: int = 0, e: Optional[int] = None, out: Optional[torch.Tensor] = None):
+        e = self.numel if e is None else e
+        if not self.split:
+            return self.f32[s:e] if out is None else out.copy_(self.f32[s:e])
+        out = torch.empty(e - s, dtype=torch.float32) if out is None else out
+        _native.host().split_to_f32(self.hi[s:e], self.lo[s:e], out)
+        return out
+
+    def write_fp32(self, src: torch.Tensor, s: int = 0) -> None:
+        e = s + src.numel()
+        src = src.reshape(-1).float().contiguous()
+        if self.split:
+            _native.host().f32_to_split(src, self.hi[s:e], self.lo[s:e])
+        else:
+            self.f32[s:e].copy_(src)
+            if self.shadow is not self.f32:
+                _native.host().cast_(self.shadow[s:e], self.f32[s:e], 1.0)
+
+    def optim_slice(self, s: int, e: int):
+        return (self.hi[s:e], self.lo[s:e]) if self.split else self.f32[s:e]

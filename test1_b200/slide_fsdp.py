@@ -53,7 +53,7 @@ from .optim.layer_adam import LayerAdam
 from .parallel.comm import CpuReduceSlots, make_comm
 from .runtime.activations import ActivationStore
 from .runtime.device import Event, Stream
-from .runtime.host_memory import HostRegion, RegionPlanner
+from .runtime.host_memory import HostRegion, MasterStore, RegionPlanner
 from .runtime.layer_state import (LayerBufferPool, LayerLayout, LayerRuntimeState, build_layout,
                                   shard_size)
 from .runtime.update import UpdateScheduler
@@ -161,13 +161,17 @@ class SlideFSDP(nn.Module):
         plan = RegionPlanner(align=4096)
         n_counters = 4 * self.num_layers + 64
         self._ctr_off = plan.take(8 * n_counters)
+        self.split_master = self.dtype == torch.bfloat16 and config.master_layout == "split"
+        want_shadow = self.dtype != torch.float32
         for l in self.layouts:
             l.master_off = plan.take(4 * l.numel)
         for l in self.layouts:
-            l.shadow_off = plan.take(2 * l.numel)
+            _, sb = MasterStore.bytes_needed(l.numel, self.split_master, want_shadow)
+            l.shadow_off = plan.take(sb) if sb else None
         dec_caps = [l.numel for l in self.layouts if l.kind == "decoder"]
         big_caps = [l.numel for l in self.layouts if l.kind != "decoder"]
-        self._slot_cap = max(dec_caps + big_caps)
+        # slot capacity rounded to 4096 elements: every slot starts on a page
+        self._slot_cap = -(-max(dec_caps + big_caps) // 4096) * 4096
         self._n_slots = 4
         self._slots_off = None
         if self.world_size > 1 and config.grad_sync_mode == "cpu_reduce":
@@ -196,12 +200,14 @@ class SlideFSDP(nn.Module):
         self.cpu_slots = cpu_slots
         self.comm = make_comm(config, self.device, self.rank, self.world_size, cpu_slots)
 
-        # ---- master init (rank 0 writes), shadow cast, then everyone pins
+        # ---- master stores; init (rank 0 writes), then everyone pins
+        self.stores = [MasterStore(self.shared, l.numel, l.master_off, self.split_master, self.dtype,
+                                   l.shadow_off) for l in self.layouts]
         self._init_master(model)
         if self.world_size > 1:
             dist.barrier()
         if self.is_cuda:
-            self.shared.pin()
+            self.shared.pin(self._pin_ranges(n_counters))
 
         # ---- per-rank host gradients (this rank's update range of each layer)
         gplan = RegionPlanner(align=4096)
@@ -210,19 +216,20 @@ class SlideFSDP(nn.Module):
             s, e = self.comm.update_range(l.numel)
             gbytes = torch.tensor([], dtype=self.dtype).element_size()
             self._grad_offs.append((gplan.take(gbytes * max(e - s, 0)), max(e - s, 0)))
-        self.grad_region = HostRegion(max(gplan.size, 4096), pin=self.is_cuda)
+        self.grad_region = HostRegion(max(gplan.size, 4096), pin=False)
+        if self.is_cuda:
+            gb = torch.tensor([], dtype=self.dtype).element_size()
+            self.grad_region.pin([(off, n * gb) for off, n in self._grad_offs if n])
 
         # ---- runtime states
         self.layer_states: List[LayerRuntimeState] = []
-        for l, (kind, mod) in zip(self.layouts, self._layer_modules()):
-            master = self.shared.view(torch.float32, l.master_off, l.numel)
-            shadow = self.shared.view(self.dtype if self.dtype != torch.float32 else torch.float32,
-                                      l.shadow_off, l.numel) if self.dtype != torch.float32 else None
+        for l, (kind, mod), store in zip(self.layouts, self._layer_modules(), self.stores):
             goff, gn = self._grad_offs[l.idx]
             grad_host = self.grad_region.view(self.dtype if self.dtype != torch.float32 else torch.float32,
                                               goff, gn) if gn else None
-            st = LayerRuntimeState(l, mod, master, shadow if shadow is not None else master,
-                                   grad_host, self.comm.update_range(l.numel))
+            st = LayerRuntimeState(l, mod, store.bind_tensor, store.shadow, grad_host,
+                                   self.comm.update_range(l.numel))
+            st.store = store
             st.bind_host()
             self.layer_states.append(st)
 
@@ -259,6 +266,21 @@ class SlideFSDP(nn.Module):
             self._print_model_info()
 
     # ------------------------------------------------------------ set-up
+    def _pin_ranges(self, n_counters: int) -> list:
+        """(offset, bytes) of every tensor of the shared region, registered
+        one by one (all start on 4096-byte boundaries)."""
+        r = [(self._ctr_off, 8 * n_counters)]
+        for l in self.layouts:
+            r.append((l.master_off, 4 * l.numel))
+            if l.shadow_off is not None:
+                r.append((l.shadow_off, 2 * l.numel))
+        if self._slots_off is not None:
+            es = torch.tensor([], dtype=self.dtype).element_size()
+            slot_bytes = self._slot_cap * es
+            for k in range(self._n_slots * self.world_size):
+                r.append((self._slots_off + k * slot_bytes, slot_bytes))
+        return r
+
     def _make_session_id(self) -> str:
         sid = [uuid.uuid4().hex[:12]]
         if self.world_size > 1:
@@ -293,7 +315,7 @@ class SlideFSDP(nn.Module):
         for st in self.layer_states:
             s, e = st.shard
             if e > s:
-                opt.add_flat_layer(st.idx, st.master[s:e])
+                opt.add_flat_layer(st.idx, st.store.optim_slice(s, e))
                 n += 1
         return opt if n else None
 
@@ -308,27 +330,26 @@ class SlideFSDP(nn.Module):
         std = self.model_config.initializer_range
         seed = self.config.seed
         gen_dev = self.device if self.is_cuda else torch.device("cpu")
-        for l in self.layouts:
-            master = self.shared.view(torch.float32, l.master_off, l.numel)
+        chunk = 1 << 26
+        staging = torch.empty(chunk, dtype=torch.float32, pin_memory=self.is_cuda)
+        for l, store in zip(self.layouts, self.stores):
             for k, e in enumerate(l.entries):
-                dst = master[e.offset:e.offset + e.numel]
                 p = e.param
                 if p.device.type == "meta":
                     if e.name.endswith("norm.weight") or e.name.endswith("layernorm.weight"):
-                        dst.fill_(1.0)
+                        for c0 in range(0, e.numel, chunk):
+                            c1 = min(e.numel, c0 + chunk)
+                            store.write_fp32(staging[: c1 - c0].fill_(1.0), e.offset + c0)
                     else:
                         g = torch.Generator(device=gen_dev)
                         g.manual_seed(seed * 1_000_003 + l.idx * 7919 + k)
-                        chunk = 1 << 26
                         for c0 in range(0, e.numel, chunk):
                             c1 = min(e.numel, c0 + chunk)
                             r = torch.randn(c1 - c0, generator=g, device=gen_dev, dtype=torch.float32)
-                            dst[c0:c1].copy_(r.mul_(std))
+                            staging[: c1 - c0].copy_(r.mul_(std))
+                            store.write_fp32(staging[: c1 - c0], e.offset + c0)
                 else:
-                    dst.copy_(p.detach().reshape(-1).float())
-            if self.dtype != torch.float32:
-                shadow = self.shared.view(self.dtype, l.shadow_off, l.numel)
-                host.cast_(shadow, master, 1.0)
+                    store.write_fp32(p.detach().reshape(-1).float(), e.offset)
 
     def _print_model_info(self) -> None:
         gb = 1e9
@@ -414,7 +435,8 @@ class SlideFSDP(nn.Module):
         s, e = st.shard
         has_work = opt is not None and e > s
         scale = self.comm.grad_scale
-        shadow = st.shadow[s:e] if (has_work and self.dtype != torch.float32) else None
+        shadow = (st.shadow[s:e] if (has_work and self.dtype != torch.float32 and not st.store.split)
+                  else None)
 
         def run_update(grad=None):
             if has_work:
@@ -612,15 +634,12 @@ class SlideFSDP(nn.Module):
         return torch.tensor(total)
 
     # --------------------------------------------------------- persistence
-    def _gather_full_param(self, st: LayerRuntimeState) -> torch.Tensor:
-        return st.master  # shared host memory holds every rank's updates
-
     def named_master_tensors(self):
         """(HF name, fp32 host view) for every parameter, in model order."""
         prefix = {"embed": "model.embed_tokens.", "output": ""}
         out = []
         for st in self.layer_states:
-            views = st.layout.views(st.master)
+            views = st.layout.views(st.store.read_fp32())
             for e in st.layout.entries:
                 if st.kind == "embed":
                     name = "model.embed_tokens." + e.name
@@ -654,7 +673,7 @@ class SlideFSDP(nn.Module):
         os.makedirs(directory, exist_ok=True)
         if self.rank == 0:
             for st in self.layer_states:
-                torch.save(st.master.clone(), os.path.join(directory, f"layer_{st.idx}.pt"))
+                torch.save(st.store.read_fp32().clone(), os.path.join(directory, f"layer_{st.idx}.pt"))
             with open(os.path.join(directory, "manifest.json"), "w") as f:
                 json.dump({"world_size": self.world_size, "completed_steps": self.completed_steps,
                            "optimizer_sharding": self.config.optimizer_sharding,
@@ -679,9 +698,7 @@ class SlideFSDP(nn.Module):
         host = _native.host()
         if self.rank == 0:
             for st in self.layer_states:
-                st.master.copy_(torch.load(os.path.join(directory, f"layer_{st.idx}.pt")))
-                if self.dtype != torch.float32:
-                    host.cast_(st.shadow, st.master, 1.0)
+                st.store.write_fp32(torch.load(os.path.join(directory, f"layer_{st.idx}.pt")))
         if self.layer_optimizer is not None:
             for st in self.layer_states:
                 if st.shard[1] > st.shard[0]:
