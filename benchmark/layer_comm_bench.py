@@ -1,0 +1,173 @@
+"""Per-layer communication microbenchmark for one
+Llama-3.1-8B decoder layer (218,112,000 params, bf16 on the GPU), 2..8 GPUs:
+
+  (a) shard fetch: this rank's 1/N shard of the fp32 master (split layout,
+      page-locked host memory) -> bf16 on every GPU, fused with the QKV GEMM
+      on activations [4096 tokens x 4096]   -- fused_ag_qkv
+      vs. NCCL path: H2D of the fp32 shard + cast + all_gather_into_tensor
+      + cuBLAS QKV GEMM
+  (b) gradient reduce-scatter + 1/N scale + copy into the page-locked host
+      shard                                  -- fused_rs_d2h
+      vs. NCCL path: reduce_scatter_tensor + scale + D2H copy
+  (c) LayerAdam host step on this rank's shard of the layer
+
+Roofline per fused path = the slowest of: FLOPs / measured bf16 peak, bytes
+crossing PCIe / 55 GB/s (measured per-direction host link on this pool), bytes
+crossing NVLink / 770 GB/s per direction per GPU.  Timed with CUDA events after
+warm-up; every rank reports, rank 0 prints the max over ranks.
+
+    torchrun --nnodes=1 --nproc-per-node 2 --master-addr 127.0.0.1 benchmark/layer_comm_bench.py
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+import time
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+PCIE_GBS = 55.0
+NVLINK_GBS = 770.0
+
+
+def peak_tflops():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)["bf16_tflops"], "of measured"
+    except Exception:
+        return 1590.0, "of fallback"
+
+
+def timed(fn, iters=5, warmup=2):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def maxr(x):
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main():
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    from test1_b200 import _native
+    from test1_b200.parallel.fused import SymmetricBuffer
+    from test1_b200.runtime.host_memory import HostRegion
+    from test1_b200.runtime.layer_state import shard_bounds, shard_size
+
+    C = _native.cuda()
+    H, I, Hq, Hkv, D = 4096, 14336, 32, 8, 128
+    n_qkv = (Hq + 2 * Hkv) * D
+    P = H * n_qkv + Hq * D * H + 3 * H * I + 2 * H
+    T = 4096
+    peak, tag = peak_tflops()
+    s, e = shard_bounds(P, world, rank)
+    n = e - s
+    ss = shard_size(P, world)
+
+    # host shard of the split master, page-locked and mapped
+    region = HostRegion(4 * n + 4096)
+    hi = region.view(torch.bfloat16, 0, n)
+    lo = region.view(torch.int16, 2 * n, n)
+    _native.host().f32_to_split(torch.randn(n) * 0.02, hi, lo)
+    region.pin([(0, 4 * n)])
+    grad_host = torch.empty(n, dtype=torch.bfloat16, pin_memory=True)
+
+    unit = SymmetricBuffer(world * ss, torch.bfloat16, dev, dist.group.WORLD)
+    gbuf = SymmetricBuffer(world * ss, torch.bfloat16, dev, dist.group.WORLD)
+    gbuf.tensor.normal_()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    shards = torch.tensor([list(shard_bounds(P, world, q)) for q in range(world)], dtype=torch.int64)
+    x = torch.randn(T, H, device=dev).bfloat16()
+    qkv = torch.empty(T, n_qkv, device=dev, dtype=torch.bfloat16)
+
+    def fused_a():
+        C.fused_ag_qkv(x, unit.tensor, n_qkv, qkv, unit.ptrs, unit.sigs, shards, rank, world,
+                       hi, lo, unit.next_epoch(), unit.ag_counters)
+
+    f32_dev = torch.empty(ss, device=dev, dtype=torch.float32)
+    gathered = torch.empty(world * ss, device=dev, dtype=torch.bfloat16)
+    master_f32 = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    _native.host().split_to_f32(hi, lo, master_f32)
+
+    def nccl_a():
+        f32_dev[:n].copy_(master_f32, non_blocking=True)
+        mine = gathered[rank * ss:(rank + 1) * ss]
+        mine.copy_(f32_dev)
+        dist.all_gather_into_tensor(gathered, mine)
+        torch.matmul(x, gathered[: n_qkv * H].view(n_qkv, H).t(), out=qkv)
+
+    def fused_b():
+        C.fused_rs_d2h(gbuf.ptrs, gbuf.sigs, rank, world, s, n, grad_host, 1.0 / world,
+                       gbuf.next_epoch(), gbuf.counter, err)
+
+    rs_out = torch.empty(ss, device=dev, dtype=torch.bfloat16)
+
+    def nccl_b():
+        dist.reduce_scatter_tensor(rs_out, gbuf.tensor[: world * ss])
+        rs_out.mul_(1.0 / world)
+        grad_host[:n].copy_(rs_out[:n], non_blocking=True)
+
+    ta = maxr(timed(fused_a))
+    tna = maxr(timed(nccl_a))
+    tb = maxr(timed(fused_b))
+    tnb = maxr(timed(nccl_b))
+    code = int(err.item())
+
+    # (c) host LayerAdam on this rank's shard (split master, bf16 grad)
+    m = torch.zeros(n)
+    v = torch.zeros(n)
+    g = torch.randn(n).bfloat16()
+    t0 = time.perf_counter()
+    for step in range(1, 4):
+        _native.host().adam_step_split(hi, lo, g, m, v, step, 1e-5, 0.9, 0.999, 1e-8, 0.01, True, True, 1.0)
+    tc = maxr((time.perf_counter() - t0) / 3 * 1e3)
+
+    flops = 2.0 * T * n_qkv * H
+    pcie_a = 4.0 * n  # fp32 master bytes (both planes) over this rank's host link
+    nvl_a = 2.0 * P * (world - 1) / world  # bf16 bytes each GPU receives from peers
+    roof_a = max(flops / (peak * 1e12), pcie_a / (PCIE_GBS * 1e9), nvl_a / (NVLINK_GBS * 1e9)) * 1e3
+    pcie_b = 2.0 * n
+    nvl_b = 2.0 * n * (world - 1)  # each GPU pulls its shard from N-1 peers
+    roof_b = max(pcie_b / (PCIE_GBS * 1e9), nvl_b / (NVLINK_GBS * 1e9)) * 1e3
+    if rank == 0:
+        out = {
+            "n_gpus": world, "layer_params": P, "error_word": code,
+            "a_fused_ag_qkv_ms": round(ta, 3), "a_nccl_h2d_allgather_cublas_ms": round(tna, 3),
+            "a_roofline_ms": round(roof_a, 3), "a_frac_of_roofline": round(roof_a / ta, 3),
+            "b_fused_rs_d2h_ms": round(tb, 3), "b_nccl_reduce_scatter_d2h_ms": round(tnb, 3),
+            "b_roofline_ms": round(roof_b, 3), "b_frac_of_roofline": round(roof_b / tb, 3),
+            "c_layeradam_shard_ms": round(tc, 2),
+            "roofline_inputs": {"pcie_gbs": PCIE_GBS, "nvlink_gbs": NVLINK_GBS, "bf16_tflops": peak,
+                                "peak_ref": tag},
+        }
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    region.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

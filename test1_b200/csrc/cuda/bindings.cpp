@@ -31,11 +31,13 @@ void fused_rs_d2h(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t 
                   int64_t offset, int64_t n, torch::Tensor host_out, double scale, int64_t epoch,
                   torch::Tensor counter, torch::Tensor err);
 void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t world,
-                        int64_t offset, int64_t n, torch::Tensor host_src, int64_t epoch,
+                        int64_t offset, int64_t n, torch::Tensor host_src,
+                        c10::optional<torch::Tensor> host_src_lo, int64_t epoch,
                         torch::Tensor counter, torch::Tensor err);
 void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Tensor out,
                   torch::Tensor ptrs, torch::Tensor sigs, torch::Tensor shards, int64_t rank,
-                  int64_t world, torch::Tensor host_src, int64_t epoch, torch::Tensor counters);
+                  int64_t world, torch::Tensor host_src, c10::optional<torch::Tensor> host_src_lo,
+                  int64_t epoch, torch::Tensor counters);
 }  // namespace t1
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

@@ -24,7 +24,8 @@ torch::Tensor& gemm_error_word();
 // layer (identical on all ranks); host_src is this rank's shard.
 void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Tensor out,
                   torch::Tensor ptrs, torch::Tensor sigs, torch::Tensor shards, int64_t rank,
-                  int64_t world, torch::Tensor host_src, int64_t epoch, torch::Tensor counters) {
+                  int64_t world, torch::Tensor host_src, c10::optional<torch::Tensor> host_src_lo,
+                  int64_t epoch, torch::Tensor counters) {
   T1_CHECK_INPUT(x, torch::kBFloat16);
   T1_CHECK_INPUT(unit, torch::kBFloat16);
   T1_CHECK_INPUT(out, torch::kBFloat16);
@@ -49,8 +50,10 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
                   sigs.numel() == world, "peer tables must be CPU int64 [world]");
   TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == torch::kInt32 &&
                   counters.numel() >= gemm::kAgMaxBlocks + 1, "counters must be int32 [65] on the GPU");
-  TORCH_CHECK(host_src.scalar_type() == torch::kFloat32 || host_src.scalar_type() == torch::kBFloat16,
-              "host_src must be fp32 or bf16");
+  const bool split = host_src_lo.has_value() && host_src_lo->defined();
+  TORCH_CHECK(split || host_src.scalar_type() == torch::kFloat32 ||
+                  host_src.scalar_type() == torch::kBFloat16,
+              "host_src must be fp32, bf16, or the high plane of a split master");
   TORCH_CHECK(host_src.numel() >= shard_n && host_src.is_contiguous(), "host_src too small");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(host_src.data_ptr()) % 16 == 0, "host_src misaligned");
 
@@ -74,7 +77,19 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
     src = d;
   }
   ag.host_src = src;
-  ag.src_f32 = host_src.scalar_type() == torch::kFloat32 ? 1 : 0;
+  ag.host_src_lo = nullptr;
+  if (split) {
+    TORCH_CHECK(host_src.element_size() == 2 && host_src_lo->element_size() == 2 &&
+                    host_src_lo->numel() >= shard_n && host_src_lo->is_contiguous() &&
+                    reinterpret_cast<uintptr_t>(host_src_lo->data_ptr()) % 16 == 0,
+                "bad split-master low plane");
+    void* d = host_src_lo->data_ptr();
+    if (host_src_lo->device().is_cpu()) T1_CHECK_CUDA(cudaHostGetDevicePointer(&d, host_src_lo->data_ptr(), 0));
+    ag.host_src_lo = d;
+    ag.src_kind = 2;
+  } else {
+    ag.src_kind = host_src.scalar_type() == torch::kFloat32 ? 1 : 0;
+  }
   ag.epoch = static_cast<uint32_t>(epoch);
   ag.n_blocks = static_cast<int>(n_blocks);
   ag.block_elems = static_cast<long>(gemm::BN) * K;

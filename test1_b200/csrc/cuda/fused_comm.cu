@@ -134,9 +134,50 @@ __global__ void __launch_bounds__(256) rs_d2h_kernel(Peers pe, int rank, int wor
 }
 
 // ------------------------------------------------------------ shard gather
-template <bool SRC_F32>
+// Source kinds: 0 = bf16 copy, 1 = fp32 master, 2 = split fp32 master (a
+// bf16-rounded high plane and a 16-bit low plane, value =
+// ((hi << 16) | lo) - 0x8000).  Kinds 1 and 2 are cast to bf16 (nearest
+// even) here.
+enum SrcKind : int { kSrcBf16 = 0, kSrcF32 = 1, kSrcSplit = 2 };
+
+__device__ __forceinline__ int4 load8_as_bf16(int kind, const void* src, const void* src_lo, long e) {
+  int4 out;
+  if (kind == kSrcBf16) {
+    out = *reinterpret_cast<const int4*>(static_cast<const bf16*>(src) + e);
+    return out;
+  }
+  float f[8];
+  if (kind == kSrcF32) {
+    const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(src) + e);
+    float4 a = s[0], b = s[1];
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    int4 hv = *reinterpret_cast<const int4*>(static_cast<const uint16_t*>(src) + e);
+    int4 lv = *reinterpret_cast<const int4*>(static_cast<const uint16_t*>(src_lo) + e);
+    const uint16_t* h = reinterpret_cast<const uint16_t*>(&hv);
+    const uint16_t* l = reinterpret_cast<const uint16_t*>(&lv);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      f[k] = __uint_as_float(((static_cast<uint32_t>(h[k]) << 16) | l[k]) - 0x8000u);
+  }
+  __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) o[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+  return out;
+}
+
+__device__ __forceinline__ bf16 load1_as_bf16(int kind, const void* src, const void* src_lo, long e) {
+  if (kind == kSrcBf16) return static_cast<const bf16*>(src)[e];
+  if (kind == kSrcF32) return __float2bfloat16_rn(static_cast<const float*>(src)[e]);
+  const uint32_t b = ((static_cast<uint32_t>(static_cast<const uint16_t*>(src)[e]) << 16) |
+                      static_cast<const uint16_t*>(src_lo)[e]) - 0x8000u;
+  return __float2bfloat16_rn(__uint_as_float(b));
+}
+
 __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, int world, long offset,
-                                                           long n, const void* __restrict__ host_src,
+                                                           long n, int kind, const void* __restrict__ host_src,
+                                                           const void* __restrict__ host_src_lo,
                                                            uint32_t epoch, int* counter, int* err) {
   // my unit is free (stream order): announce it, wait until every peer's is
   if (blockIdx.x == 0 && threadIdx.x == 0) signal_all(pe, rank, world, epoch);
@@ -145,18 +186,7 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, i
   const long n8 = n >> 3;
   const long stride = static_cast<long>(gridDim.x) * blockDim.x;
   for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
-    int4 out;
-    if (SRC_F32) {
-      const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(host_src) + 8 * i);
-      float4 a = s[0], b = s[1];
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
-      h[0] = __floats2bfloat162_rn(a.x, a.y);
-      h[1] = __floats2bfloat162_rn(a.z, a.w);
-      h[2] = __floats2bfloat162_rn(b.x, b.y);
-      h[3] = __floats2bfloat162_rn(b.z, b.w);
-    } else {
-      out = *reinterpret_cast<const int4*>(static_cast<const bf16*>(host_src) + 8 * i);
-    }
+    const int4 out = load8_as_bf16(kind, host_src, host_src_lo, 8 * i);
 #pragma unroll 1
     for (int p = 0; p < world; ++p) {
       bf16* dst = reinterpret_cast<bf16*>(pe.ptr[p]) + offset + 8 * i;
@@ -165,8 +195,7 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, i
   }
   if (blockIdx.x == 0) {
     for (long j = (n8 << 3) + threadIdx.x; j < n; j += blockDim.x) {
-      bf16 v = SRC_F32 ? __float2bfloat16_rn(static_cast<const float*>(host_src)[j])
-                       : static_cast<const bf16*>(host_src)[j];
+      const bf16 v = load1_as_bf16(kind, host_src, host_src_lo, j);
       for (int p = 0; p < world; ++p) reinterpret_cast<bf16*>(pe.ptr[p])[offset + j] = v;
     }
   }
@@ -220,31 +249,43 @@ void fused_rs_d2h(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t 
   count_launch();
 }
 
+// Device view of a page-locked host tensor (UVA: the host address itself).
+static const void* device_view(const torch::Tensor& t) {
+  if (!t.device().is_cpu()) return t.data_ptr();
+  void* d = nullptr;
+  T1_CHECK_CUDA(cudaHostGetDevicePointer(&d, t.data_ptr(), 0));
+  return d;
+}
+
+// host_src: this rank's shard: fp32 master, bf16 copy, or (with host_src_lo)
+// the high plane of a split master.
 void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t world,
-                        int64_t offset, int64_t n, torch::Tensor host_src, int64_t epoch,
+                        int64_t offset, int64_t n, torch::Tensor host_src,
+                        c10::optional<torch::Tensor> host_src_lo, int64_t epoch,
                         torch::Tensor counter, torch::Tensor err) {
   auto pe = make_peers(ptrs, sigs, world);
   TORCH_CHECK(host_src.is_contiguous() && host_src.numel() >= n, "host_src too small");
-  TORCH_CHECK(host_src.scalar_type() == torch::kFloat32 || host_src.scalar_type() == torch::kBFloat16,
-              "host_src must be fp32 (master) or bf16 (shadow)");
   TORCH_CHECK(offset % 8 == 0, "shard offset must be a multiple of 8 elements");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(host_src.data_ptr()) % 16 == 0, "host_src misaligned");
-  if (n <= 0) return;
-  const void* src_dev = host_src.data_ptr();
-  if (host_src.device().is_cpu()) {
-    void* d = nullptr;
-    T1_CHECK_CUDA(cudaHostGetDevicePointer(&d, host_src.data_ptr(), 0));
-    src_dev = d;
+  int kind;
+  const void* lo = nullptr;
+  if (host_src_lo.has_value() && host_src_lo->defined()) {
+    TORCH_CHECK(host_src.element_size() == 2 && host_src_lo->element_size() == 2 &&
+                    host_src_lo->is_contiguous() && host_src_lo->numel() >= n,
+                "split master planes must be 16-bit tensors of >= n elements");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(host_src_lo->data_ptr()) % 16 == 0, "low plane misaligned");
+    kind = fused::kSrcSplit;
+    lo = device_view(*host_src_lo);
+  } else if (host_src.scalar_type() == torch::kFloat32) {
+    kind = fused::kSrcF32;
+  } else {
+    TORCH_CHECK(host_src.scalar_type() == torch::kBFloat16, "host_src must be fp32 or bf16");
+    kind = fused::kSrcBf16;
   }
-  const int grid = comm_grid(n / 8);
-  if (host_src.scalar_type() == torch::kFloat32)
-    fused::shard_gather_kernel<true><<<grid, 256, 0, stream()>>>(
-        pe, rank, world, offset, n, src_dev, static_cast<uint32_t>(epoch), counter.data_ptr<int>(),
-        err.data_ptr<int>());
-  else
-    fused::shard_gather_kernel<false><<<grid, 256, 0, stream()>>>(
-        pe, rank, world, offset, n, src_dev, static_cast<uint32_t>(epoch), counter.data_ptr<int>(),
-        err.data_ptr<int>());
+  if (n <= 0) return;
+  fused::shard_gather_kernel<<<comm_grid(n / 8), 256, 0, stream()>>>(
+      pe, rank, world, offset, n, kind, device_view(host_src), lo, static_cast<uint32_t>(epoch),
+      counter.data_ptr<int>(), err.data_ptr<int>());
   check_launch("fused_shard_gather");
   count_launch();
 }

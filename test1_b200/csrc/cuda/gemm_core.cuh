@@ -45,8 +45,9 @@ struct AgParams {
   uint64_t sig[kAgMaxRanks];   // every rank's signal pad for that buffer
   int rank, world;
   long shard_off, shard_n;     // this rank's shard of the layer (elements)
-  const void* host_src;        // device view of the page-locked shard (fp32 or bf16)
-  int src_f32;
+  const void* host_src;        // device view of the page-locked shard
+  const void* host_src_lo;     // split master: the low plane
+  int src_kind;                // 0 bf16 copy, 1 fp32 master, 2 split master (hi/lo planes)
   uint32_t epoch;
   int n_blocks;                // 256-row blocks of B (= the QKV weight rows / 256)
   long block_elems;            // 256 * K
@@ -95,16 +96,27 @@ __device__ __forceinline__ void ag_copy(const AgParams& ag, long b, long e, int 
   for (long v = v0 + gt; v < v1; v += 64) {
     int4 out;
     const long local = 8 * v - ag.shard_off;
-    if (ag.src_f32) {
-      const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(ag.host_src) + local);
-      float4 x = src[0], y = src[1];
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
-      h[0] = __floats2bfloat162_rn(x.x, x.y);
-      h[1] = __floats2bfloat162_rn(x.z, x.w);
-      h[2] = __floats2bfloat162_rn(y.x, y.y);
-      h[3] = __floats2bfloat162_rn(y.z, y.w);
-    } else {
+    if (ag.src_kind == 0) {
       out = *reinterpret_cast<const int4*>(static_cast<const bf16*>(ag.host_src) + local);
+    } else {
+      float f[8];
+      if (ag.src_kind == 1) {
+        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(ag.host_src) + local);
+        float4 x = src[0], y = src[1];
+        f[0] = x.x; f[1] = x.y; f[2] = x.z; f[3] = x.w;
+        f[4] = y.x; f[5] = y.y; f[6] = y.z; f[7] = y.w;
+      } else {
+        int4 hv = *reinterpret_cast<const int4*>(static_cast<const uint16_t*>(ag.host_src) + local);
+        int4 lv = *reinterpret_cast<const int4*>(static_cast<const uint16_t*>(ag.host_src_lo) + local);
+        const uint16_t* h = reinterpret_cast<const uint16_t*>(&hv);
+        const uint16_t* l = reinterpret_cast<const uint16_t*>(&lv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          f[k] = __uint_as_float(((static_cast<uint32_t>(h[k]) << 16) | l[k]) - 0x8000u);
+      }
+      __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) o[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
     }
     for (int q = 0; q < ag.world; ++q)
       *reinterpret_cast<int4*>(reinterpret_cast<bf16*>(ag.peer[q]) + 8 * v) = out;
@@ -315,8 +327,16 @@ __global__ void __launch_bounds__(AG ? 256 : 192, 1)
       if (blockIdx.x == 0) {
         for (long j = ((s1 >> 3) << 3) + gt; j < s1; j += 64) {
           const long local = j - s0;
-          bf16 v = ag.src_f32 ? __float2bfloat16_rn(static_cast<const float*>(ag.host_src)[local])
-                              : static_cast<const bf16*>(ag.host_src)[local];
+          bf16 v;
+          if (ag.src_kind == 0) {
+            v = static_cast<const bf16*>(ag.host_src)[local];
+          } else if (ag.src_kind == 1) {
+            v = __float2bfloat16_rn(static_cast<const float*>(ag.host_src)[local]);
+          } else {
+            const uint32_t b = ((static_cast<uint32_t>(static_cast<const uint16_t*>(ag.host_src)[local]) << 16) |
+                                static_cast<const uint16_t*>(ag.host_src_lo)[local]) - 0x8000u;
+            v = __float2bfloat16_rn(__uint_as_float(b));
+          }
           for (int q = 0; q < ag.world; ++q) reinterpret_cast<bf16*>(ag.peer[q])[j] = v;
         }
       }

@@ -116,10 +116,10 @@ class FusedComm(CollectiveComm):
             return super().fetch_params(st, dst, stream)
         s, e = shard_bounds(st.numel, self.world, self.rank)
         b = self._buf(dst)
-        src = self._gather_src(st, s, e)
+        src, lo = self._gather_src(st, s, e)
         with stream.ctx():
             _native.cuda().fused_shard_gather(b.ptrs, b.sigs, self.rank, self.world, s, e - s,
-                                              src, b.next_epoch(), b.counter, self.err)
+                                              src, lo, b.next_epoch(), b.counter, self.err)
 
     def sync_grads(self, st: LayerRuntimeState, src: torch.Tensor, stream: Stream) -> None:
         if not self.fused_grads:
@@ -151,21 +151,23 @@ class FusedComm(CollectiveComm):
         (one kernel, on the current stream)."""
         s, e = shard_bounds(st.numel, self.world, self.rank)
         b = self._buf(st.unit.param)
-        src = self._gather_src(st, s, e)
+        src, lo = self._gather_src(st, s, e)
         out = torch.empty(x1.shape[0], n_rows, dtype=x1.dtype, device=x1.device)
         _native.cuda().fused_ag_qkv(x1, b.tensor, n_rows, out, b.ptrs, b.sigs,
-                                    self.shard_table(st.numel), self.rank, self.world, src,
+                                    self.shard_table(st.numel), self.rank, self.world, src, lo,
                                     b.next_epoch(), b.ag_counters)
         return out
 
-    def _gather_src(self, st: LayerRuntimeState, s: int, e: int) -> torch.Tensor:
-        """What the shard fetch reads from host memory: the fp32 master (cast
-        to bf16 on the GPU) or the bf16 copy.  A split master's high plane
-        is the bf16 copy."""
+    def _gather_src(self, st: LayerRuntimeState, s: int, e: int):
+        """(tensor, low plane or None) the shard fetch reads from host
+        memory: the fp32 master -- plain, or both planes of a split master --
+        cast to bf16 (nearest even) on the GPU; or the bf16 copy."""
         store = getattr(st, "store", None)
-        if self.shard_source == "master" and store is not None and not store.split:
-            return store.f32[s:e]
-        return st.shadow[s:e]
+        if self.shard_source == "master" and store is not None:
+            if store.split:
+                return store.hi[s:e], store.lo[s:e]
+            return store.f32[s:e], None
+        return st.shadow[s:e], None
 
     def check(self) -> None:
         code = int(self.err.item())

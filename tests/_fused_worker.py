@@ -60,7 +60,20 @@ def kernels(rank, world, port, out_path):
             pbuf.tensor.zero_()
             torch.cuda.synchronize()
             dist.barrier()
-            C.fused_shard_gather(pbuf.ptrs, pbuf.sigs, rank, world, s, e - s, master[s:e],
+            C.fused_shard_gather(pbuf.ptrs, pbuf.sigs, rank, world, s, e - s, master[s:e], None,
+                                 pbuf.next_epoch(), pbuf.counter, err)
+            torch.cuda.synchronize()
+            if not torch.equal(pbuf.tensor.cpu(), master.bfloat16()):
+                ok = False
+                msgs.append(f"gather(fp32) it{it} mismatch")
+            # split master: both planes, rebuilt and rounded on the GPU
+            hi = torch.empty(P, dtype=torch.bfloat16).pin_memory()
+            lo = torch.empty(P, dtype=torch.int16).pin_memory()
+            _native.host().f32_to_split(master, hi, lo)
+            pbuf.tensor.zero_()
+            torch.cuda.synchronize()
+            dist.barrier()
+            C.fused_shard_gather(pbuf.ptrs, pbuf.sigs, rank, world, s, e - s, hi[s:e], lo[s:e],
                                  pbuf.next_epoch(), pbuf.counter, err)
             torch.cuda.synchronize()
             if not torch.equal(pbuf.tensor.cpu(), master.bfloat16()):
@@ -134,14 +147,22 @@ def ag_gemm(rank, world, port, out_path, src_kind):
         ok, msgs = True, []
         for it in range(3):
             master = torch.randn(P, generator=torch.Generator().manual_seed(31 + it)) * 0.05
-            src = (master if src_kind == "fp32" else master.bfloat16())[s:e].contiguous().pin_memory()
+            lo = None
+            if src_kind == "split":
+                hi_all = torch.empty(P, dtype=torch.bfloat16)
+                lo_all = torch.empty(P, dtype=torch.int16)
+                _native.host().f32_to_split(master, hi_all, lo_all)
+                src = hi_all[s:e].contiguous().pin_memory()
+                lo = lo_all[s:e].contiguous().pin_memory()
+            else:
+                src = (master if src_kind == "fp32" else master.bfloat16())[s:e].contiguous().pin_memory()
             x = torch.randn(T, K, generator=torch.Generator().manual_seed(77 + it)).bfloat16().to(dev)
             out = torch.empty(T, n_rows, dtype=torch.bfloat16, device=dev)
             unit.tensor.zero_()
             torch.cuda.synchronize()
             dist.barrier()
             C.fused_ag_qkv(x, unit.tensor, n_rows, out, unit.ptrs, unit.sigs, shards, rank, world,
-                           src, unit.next_epoch(), counters)
+                           src, lo, unit.next_epoch(), counters)
             torch.cuda.synchronize()
             full = master.bfloat16().to(dev)
             if not torch.equal(unit.tensor, full):

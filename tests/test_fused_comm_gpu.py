@@ -70,7 +70,7 @@ def test_engine_fused_matches_nccl(tmp_path, mode):
         assert (d > 1e-3).float().mean().item() < 0.01, n
 
 
-@pytest.mark.parametrize("src_kind", ["fp32", "bf16"])
+@pytest.mark.parametrize("src_kind", ["fp32", "bf16", "split"])
 def test_fused_ag_qkv_two_gpus(tmp_path, src_kind):
     _need2()
     from tests._fused_worker import ag_gemm
