@@ -93,6 +93,11 @@ class CommStrategy:
         with stream.ctx():
             dst[: st.numel].copy_(st.shadow, non_blocking=True)
 
+    def host_read_views(self, st: LayerRuntimeState) -> list:
+        """The host tensors this rank's GPU reads when ``fetch_params`` loads
+        layer ``st`` (the engine page-locks exactly these)."""
+        return [st.shadow]
+
     def sync_grads(self, st: LayerRuntimeState, src: torch.Tensor, stream: Stream) -> None:
         """Enqueue on ``stream`` everything that moves this rank's share of
         the layer gradient into ``st.grad_host``."""
@@ -141,6 +146,12 @@ class CollectiveComm(CommStrategy):
         if self.param_mode == "shard" or (self.grad_mode == "gpu_reduce" and not self.rank0_optimizer):
             return self.world * shard_size(numel, self.world)
         return numel
+
+    def host_read_views(self, st: LayerRuntimeState) -> list:
+        if self.param_mode == "full":
+            return super().host_read_views(st)
+        s, e = shard_bounds(st.numel, self.world, self.rank)
+        return [st.shadow[s:e]] if e > s else []
 
     def fetch_params(self, st: LayerRuntimeState, dst: torch.Tensor, stream: Stream) -> None:
         if self.param_mode == "full":

@@ -121,6 +121,14 @@ class FusedComm(CollectiveComm):
             _native.cuda().fused_shard_gather(b.ptrs, b.sigs, self.rank, self.world, s, e - s,
                                               src, lo, b.next_epoch(), b.counter, self.err)
 
+    def host_read_views(self, st: LayerRuntimeState) -> list:
+        if not self.fused_params:
+            return super().host_read_views(st)
+        s, e = shard_bounds(st.numel, self.world, self.rank)
+        if e <= s:
+            return []
+        return [t for t in self._gather_src(st, s, e) if t is not None]
+
     def sync_grads(self, st: LayerRuntimeState, src: torch.Tensor, stream: Stream) -> None:
         if not self.fused_grads:
             return super().sync_grads(st, src, stream)

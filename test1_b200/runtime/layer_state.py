@@ -51,6 +51,7 @@ class ParamEntry:
     shape: torch.Size
     numel: int
     offset: int  # element offset inside the layer's flat buffer
+    hf_name: str = ""  # full HF parameter name (generic-architecture path)
 
 
 @dataclass
@@ -168,7 +169,7 @@ class LayerRuntimeState:
                 # a deferred-initialisation model: swap in a real Parameter
                 # whose storage is the host master view
                 new = nn.Parameter(self._host_views[e.name], requires_grad=e.param.requires_grad)
-                _replace_param(self.module, e.name, new)
+                _replace_param(getattr(self.module, "params_root", self.module), e.name, new)
                 e.param = new
             else:
                 e.param.data = self._host_views[e.name]

@@ -48,6 +48,7 @@ import torch.nn as nn
 
 from . import _native, ops
 from .config import SlideFSDPConfig
+from .models import generic
 from .models.llama import LlamaConfig, LlamaDecoderLayer, LlamaForCausalLM, make_context
 from .optim.layer_adam import LayerAdam
 from .parallel.comm import CpuReduceSlots, make_comm
@@ -133,13 +134,15 @@ class SlideFSDP(nn.Module):
         if config.host_threads > 0:
             _native.host().configure_threads(config.host_threads, _native._cpu_list_from_env())
 
+        # Llama-structured models run the sm_100a layer programs; any other
+        # HF causal LM runs its own modules under autograd (models/generic.py)
+        self.generic = False
         if not isinstance(model, LlamaForCausalLM):
-            if getattr(getattr(model, "config", None), "model_type", None) in ("llama", "mistral"):
+            if generic.is_native_llama(model):
                 model = _convert_hf_llama(model)
             else:
-                raise NotImplementedError(
-                    f"SlideFSDP supports Llama-architecture causal LMs; got {type(model).__name__}")
-        if model.config.tie_word_embeddings:
+                self.generic = True
+        if getattr(model.config, "tie_word_embeddings", False):
             raise NotImplementedError("tied input/output embeddings are not supported by layer sliding")
         self.base_model = model
         self.model_config = model.config
@@ -152,7 +155,11 @@ class SlideFSDP(nn.Module):
         # ---- layouts -------------------------------------------------------
         self.layouts: List[LayerLayout] = []
         for idx, (kind, mod) in enumerate(self._layer_modules()):
-            self.layouts.append(build_layout(idx, kind, mod))
+            self.layouts.append(build_layout(idx, kind, getattr(mod, "params_root", mod)))
+        if self.generic:
+            for l in self.layouts:
+                for e in l.entries:
+                    e.hf_name = self._hf_names[id(e.param)]
         self.num_layers = len(self.layouts)
         self.total_params = sum(l.numel for l in self.layouts)
         self.max_param_size = max(l.numel for l in self.layouts)
@@ -206,8 +213,6 @@ class SlideFSDP(nn.Module):
         self._init_master(model)
         if self.world_size > 1:
             dist.barrier()
-        if self.is_cuda:
-            self.shared.pin(self._pin_ranges(n_counters))
 
         # ---- per-rank host gradients (this rank's update range of each layer)
         gplan = RegionPlanner(align=4096)
@@ -232,6 +237,10 @@ class SlideFSDP(nn.Module):
             st.store = store
             st.bind_host()
             self.layer_states.append(st)
+
+        # ---- page-lock what this rank's GPU reads or writes in the shared region
+        if self.is_cuda:
+            self.shared.pin(self._pin_ranges())
 
         # ---- optimizer (this rank's range of every layer)
         self.layer_optimizer = self._create_optimizer(config)
@@ -266,20 +275,35 @@ class SlideFSDP(nn.Module):
             self._print_model_info()
 
     # ------------------------------------------------------------ set-up
-    def _pin_ranges(self, n_counters: int) -> list:
-        """(offset, bytes) of every tensor of the shared region, registered
-        one by one (all start on 4096-byte boundaries)."""
-        r = [(self._ctr_off, 8 * n_counters)]
-        for l in self.layouts:
-            r.append((l.master_off, 4 * l.numel))
-            if l.shadow_off is not None:
-                r.append((l.shadow_off, 2 * l.numel))
+    def _pin_ranges(self) -> list:
+        """(offset, bytes) ranges of the shared region that this rank's GPU
+        touches: the host tensors its parameter fetches read (every layer's
+        bf16 copy in ``full`` mode, only its own shard in ``shard`` mode) and
+        the cpu_reduce slots.  Rounded out to pages and merged, so no two
+        registrations share a page and each copy lies in one registration.
+        Every local rank maps the same pages, so pinning only what each
+        rank reads keeps the node's page-locked total near one copy of the
+        model instead of one per GPU."""
+        base = self.shared.buf.data_ptr()
+        spans = []
+        for st in self.layer_states:
+            for t in self.comm.host_read_views(st):
+                if t.numel():
+                    off = t.data_ptr() - base
+                    spans.append((off, off + t.numel() * t.element_size()))
         if self._slots_off is not None:
             es = torch.tensor([], dtype=self.dtype).element_size()
-            slot_bytes = self._slot_cap * es
-            for k in range(self._n_slots * self.world_size):
-                r.append((self._slots_off + k * slot_bytes, slot_bytes))
-        return r
+            n = CpuReduceSlots.region_bytes(self._slot_cap, self.world_size, self._n_slots, es)
+            spans.append((self._slots_off, self._slots_off + n))
+        page = 4096
+        spans = sorted((a // page * page, min(-(-b // page) * page, self.shared.nbytes)) for a, b in spans)
+        merged = []
+        for a, b in spans:
+            if merged and a <= merged[-1][1]:
+                merged[-1][1] = max(merged[-1][1], b)
+            else:
+                merged.append([a, b])
+        return [(a, b - a) for a, b in merged]
 
     def _make_session_id(self) -> str:
         sid = [uuid.uuid4().hex[:12]]
@@ -287,13 +311,49 @@ class SlideFSDP(nn.Module):
             dist.broadcast_object_list(sid, src=0)
         return sid[0]
 
-    def _split_model(self, model: LlamaForCausalLM) -> None:
+    def _split_model(self, model: nn.Module) -> None:
+        """embedding | decoder layers | (final norm + lm_head), as the
+        reference splits any HF model (slide_fsdp.py:213-244)."""
         decoder = model.get_decoder()
-        self.embed_tokens = model.get_input_embeddings()
-        self.decoder_layers = nn.ModuleList(decoder.layers)
-        self.num_decoder_layers = len(decoder.layers)
-        self.output_layer = OutputLayer(decoder.norm, model.get_output_embeddings(),
-                                        model.config.rms_norm_eps)
+        if hasattr(decoder, "layers"):
+            layers = decoder.layers
+        elif hasattr(decoder, "block"):
+            layers = decoder.block
+        else:
+            raise ValueError("Cannot find decoder layers in model")
+        self.num_decoder_layers = len(layers)
+        self.rotary_emb = None
+        if not self.generic:
+            self.embed_tokens = model.get_input_embeddings()
+            self.decoder_layers = nn.ModuleList(layers)
+            self.output_layer = OutputLayer(decoder.norm, model.get_output_embeddings(),
+                                            model.config.rms_norm_eps)
+            return
+        self.embed_tokens = generic.GenericEmbedding(model.get_input_embeddings())
+        self.decoder_layers = nn.ModuleList(generic.GenericDecoderLayer(l) for l in layers)
+        self.output_layer = generic.GenericOutputLayer(decoder.norm, model.get_output_embeddings())
+        rot = getattr(decoder, "rotary_emb", None)
+        if rot is not None:
+            # a fresh instance on the compute device (its buffers are not
+            # parameters, and a deferred-init model has them on meta)
+            self.rotary_emb = type(rot)(model.config, device=self.device)
+        # HF names of every parameter, for checkpoints of any architecture
+        self._hf_names = {id(p): n for n, p in model.named_parameters()}
+
+    def _make_context(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor]):
+        if not self.generic:
+            return make_context(self.model_config, input_ids, labels, self.device)
+        B, S = input_ids.shape
+        ids = input_ids.to(self.device, non_blocking=True)
+        pos = torch.arange(S, device=self.device).unsqueeze(0)
+        pe = None
+        if self.rotary_emb is not None:
+            x = torch.empty(1, S, 1, device=self.device, dtype=self.dtype)
+            pe = self.rotary_emb(x, pos)
+        tg = ops.shift_labels(labels.to(self.device, non_blocking=True)) if labels is not None else None
+        masks = generic.causal_masks(self.model_config, B, S, self.model_config.hidden_size, pos,
+                                     self.device, self.dtype)
+        return generic.GenericContext(B, S, pe, pos, ids, tg, masks)
 
     def _layer_modules(self):
         out = [("embed", self.embed_tokens)]
@@ -320,7 +380,7 @@ class SlideFSDP(nn.Module):
         return opt if n else None
 
     @torch.no_grad()
-    def _init_master(self, model: LlamaForCausalLM) -> None:
+    def _init_master(self, model: nn.Module) -> None:
         """Rank 0 fills the shared fp32 master from the model's parameters
         (random N(0, initializer_range) when they are on the meta device),
         then writes the low-precision shadow."""
@@ -336,10 +396,15 @@ class SlideFSDP(nn.Module):
             for k, e in enumerate(l.entries):
                 p = e.param
                 if p.device.type == "meta":
+                    const = None
                     if e.name.endswith("norm.weight") or e.name.endswith("layernorm.weight"):
+                        const = 1.0
+                    elif e.name.endswith(".bias"):
+                        const = 0.0
+                    if const is not None:
                         for c0 in range(0, e.numel, chunk):
                             c1 = min(e.numel, c0 + chunk)
-                            store.write_fp32(staging[: c1 - c0].fill_(1.0), e.offset + c0)
+                            store.write_fp32(staging[: c1 - c0].fill_(const), e.offset + c0)
                     else:
                         g = torch.Generator(device=gen_dev)
                         g.manual_seed(seed * 1_000_003 + l.idx * 7919 + k)
@@ -481,25 +546,24 @@ class SlideFSDP(nn.Module):
         step = self.completed_steps + 1
         if self.cpu_slots is not None:
             self.cpu_slots.step = step
-        ctx = make_context(cfg, input_ids, labels, dev)
+        ctx = self._make_context(input_ids, labels)
         S = self.layer_states
         L = self.num_decoder_layers
         emb, out = S[0], S[L + 1]
 
         # ---------------- forward
         self._fetch(emb, with_grad=False)
-        fuse_first = (L > 0 and hasattr(self.comm, "can_fuse_qkv") and self.comm.can_fuse_qkv(S[1])
-                      and self.config.use_native_kernels)
+        fuse_first = (L > 0 and not self.generic and hasattr(self.comm, "can_fuse_qkv")
+                      and self.comm.can_fuse_qkv(S[1]) and self.config.use_native_kernels)
         if L > 0 and not fuse_first:
             self._fetch(S[1], with_grad=False)
         self._wait_loaded(emb)
         h = emb.module.forward_ids(ctx.input_ids)
         self._release(emb, Event(dev).record())
         prefetch = max(1, min(self.config.prefetch_layers, self.config.gpu_buffer_pool_size - 1))
-        fuse_qkv = (L > 0 and hasattr(self.comm, "can_fuse_qkv") and self.comm.can_fuse_qkv(S[1])
-                    and self.config.use_native_kernels)
+        fuse_qkv = fuse_first
         cfgm = self.model_config
-        n_qkv = cfgm.q_size + 2 * cfgm.kv_size
+        n_qkv = cfgm.q_size + 2 * cfgm.kv_size if fuse_qkv else 0
         saved_all = {}
         for i in range(1, L + 1):
             st = S[i]
@@ -571,8 +635,7 @@ class SlideFSDP(nn.Module):
     @torch.no_grad()
     def _inference(self, input_ids: torch.Tensor) -> torch.Tensor:
         """Forward only; returns logits [B, S, V]."""
-        cfg = self.model_config
-        ctx = make_context(cfg, input_ids, None, self.device)
+        ctx = self._make_context(input_ids, None)
         S = self.layer_states
         L = self.num_decoder_layers
         self._fetch(S[0], with_grad=False)
@@ -636,12 +699,13 @@ class SlideFSDP(nn.Module):
     # --------------------------------------------------------- persistence
     def named_master_tensors(self):
         """(HF name, fp32 host view) for every parameter, in model order."""
-        prefix = {"embed": "model.embed_tokens.", "output": ""}
         out = []
         for st in self.layer_states:
             views = st.layout.views(st.store.read_fp32())
             for e in st.layout.entries:
-                if st.kind == "embed":
+                if self.generic:
+                    name = e.hf_name
+                elif st.kind == "embed":
                     name = "model.embed_tokens." + e.name
                 elif st.kind == "output":
                     name = ("model." + e.name) if e.name.startswith("norm.") else e.name
@@ -658,12 +722,16 @@ class SlideFSDP(nn.Module):
 
         self.wait_for_updates()
         if self.rank == 0:
-            save_hf_checkpoint(output_dir, self.model_config.to_hf_dict(),
+            save_hf_checkpoint(output_dir, self._hf_config_dict(),
                                dict(self.named_master_tensors()), self.dtype)
             print(f"Model saved to {output_dir}")
         if self.world_size > 1:
             dist.barrier()
         return output_dir
+
+    def _hf_config_dict(self) -> dict:
+        cfg = self.model_config
+        return cfg.to_hf_dict() if hasattr(cfg, "to_hf_dict") else cfg.to_dict()
 
     def save_state(self, directory: str) -> None:
         """fp32 master (rank 0) + this rank's optimizer shards, one file per
@@ -678,7 +746,7 @@ class SlideFSDP(nn.Module):
                 json.dump({"world_size": self.world_size, "completed_steps": self.completed_steps,
                            "optimizer_sharding": self.config.optimizer_sharding,
                            "num_layers": self.num_layers, "config": self.config.to_dict(),
-                           "model": self.model_config.to_hf_dict()}, f, indent=2, default=str)
+                           "model": self._hf_config_dict()}, f, indent=2, default=str)
         if self.layer_optimizer is not None:
             for st in self.layer_states:
                 if st.shard[1] > st.shard[0]:
