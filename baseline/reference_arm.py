@@ -53,7 +53,7 @@ def _tuple_layers(model):
     return model
 
 
-def build_hf_model(model_name: str, device_for_init):
+def build_hf_model(model_name: str, device_for_init, tuple_layers: bool = True):
     import torch
     from transformers import LlamaConfig, LlamaForCausalLM
 
@@ -93,7 +93,7 @@ def build_hf_model(model_name: str, device_for_init):
                 r = torch.randn(p.shape, generator=gen, device=device_for_init, dtype=torch.float32)
                 p.copy_((r * ours.initializer_range).to(torch.bfloat16).cpu())
     model.config._attn_implementation = attn
-    return _tuple_layers(model), attn
+    return (_tuple_layers(model) if tuple_layers else model), attn
 
 
 def run(args, rank, world, local):

@@ -1,7 +1,7 @@
 """Headline benchmark: Llama-3.1-8B-architecture layer-sliding training,
 tokens/s over all GPUs (device-timed, max over ranks).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|fsdp]
     torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
 Config: Llama-3.1-8B architecture, random-init N(0,0.02)
@@ -39,7 +39,7 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=4)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--impl", choices=["ours", "reference", "fsdp"], default="ours")
     p.add_argument("--model", default="llama31_8b", choices=["llama31_8b", "tiny", "llama_70b"])
     p.add_argument("--batch", type=int, default=4)
     p.add_argument("--seq", type=int, default=1024)
@@ -255,11 +255,16 @@ def main():
     rank, world, local = init_dist(args)
     import torch
 
-    if args.impl == "reference":
-        res = run_reference(args, rank, world, local)
+    if args.impl in ("reference", "fsdp"):
+        if args.impl == "reference":
+            res = run_reference(args, rank, world, local)
+        else:
+            from baseline.fsdp_arm import run as fsdp_run
+
+            res = fsdp_run(args, rank, world, local)
         if res.get("unavailable"):
             if rank == 0:
-                print(json.dumps({"impl": "reference", "unavailable": res["unavailable"]}), flush=True)
+                print(json.dumps({"impl": args.impl, "unavailable": res["unavailable"]}), flush=True)
             return
     else:
         res = run_ours(args, rank, world, local)
@@ -291,8 +296,10 @@ def main():
         "e2e": res.get("e2e"),
         "gpu_launches": res.get("launches"),
     }
-    if args.impl == "reference":
-        line["impl"] = "reference"
+    if args.impl != "ours":
+        line["impl"] = args.impl
+        if args.impl == "fsdp":
+            line["config"]["parallelism"] = f"fsdp{world} full_shard, CPU-offloaded params, torch AdamW"
     extra = {k: res[k] for k in ("init_s", "h2d_gb_per_step", "adam_busy_s_per_step",
                                  "fetch_blocked_on_adam_s_per_step", "comm", "losses",
                                  "attn_implementation") if k in res}

@@ -38,6 +38,10 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
                   torch::Tensor ptrs, torch::Tensor sigs, torch::Tensor shards, int64_t rank,
                   int64_t world, torch::Tensor host_src, c10::optional<torch::Tensor> host_src_lo,
                   int64_t epoch, torch::Tensor counters);
+void multi_tensor_adam(int64_t chunk_size, torch::Tensor noop_flag,
+                       std::vector<std::vector<torch::Tensor>> tensor_lists, double lr, double beta1,
+                       double beta2, double eps, int64_t step, int64_t mode, int64_t bias_correction,
+                       double weight_decay);
 }  // namespace t1
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -59,4 +63,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_rs_d2h", &t1::fused_rs_d2h);
   m.def("fused_shard_gather", &t1::fused_shard_gather);
   m.def("fused_ag_qkv", &t1::fused_ag_qkv);
+  m.def("multi_tensor_adam", &t1::multi_tensor_adam,
+        "Adam/AdamW update of lists [grads, params, exp_avgs, exp_avg_sqs] (one launch per 192 tensors)");
 }
