@@ -23,6 +23,10 @@ Extra fields (all optional, reference configs never set them):
         shadow.  Only bf16 training uses "split".
     host_wait_timeout_s: bound on every host-side wait for another rank
         (optimizer publication, cpu_reduce slots); expiry raises TimeoutError.
+    trace_path: append one JSON line per training step with per-phase
+        device times (h2d, fwd, bwd, loss, grad_sync) and host optimizer
+        spans (utils/trace.py); each rank writes ``<path>.rank<r>`` when
+        there are several.
     use_native_kernels: run the model on the sm_100a kernels (True) or on
         plain PyTorch ops (False; the CPU test path).
 """
@@ -89,6 +93,7 @@ class SlideFSDPConfig:
     host_wait_timeout_s: float = 600.0  # bound on every host wait for a peer rank
     master_layout: str = "split"  # "split" (hi/lo 16-bit planes) or "fp32" (plain fp32 + bf16 shadow)
     use_native_kernels: Optional[bool] = None  # None: native iff device is CUDA
+    trace_path: Optional[str] = None  # per-phase step trace (JSON lines); env T1_TRACE also enables it
 
     def __post_init__(self):
         if self.param_transfer_mode not in ("full", "shard"):

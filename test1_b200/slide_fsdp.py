@@ -55,6 +55,7 @@ from .parallel.comm import CpuReduceSlots, make_comm
 from .runtime.activations import ActivationStore
 from .runtime.device import Event, Stream
 from .runtime.host_memory import HostRegion, MasterStore, RegionPlanner
+from .utils.trace import PhaseTracer
 from .runtime.layer_state import (LayerBufferPool, LayerLayout, LayerRuntimeState, build_layout,
                                   shard_size)
 from .runtime.update import UpdateScheduler
@@ -266,6 +267,10 @@ class SlideFSDP(nn.Module):
                          if cpu_slots is not None else None)
         self.acts = ActivationStore(config.ac_offload_mode if config.enable_activation_checkpoint else "gpu",
                                     self.device, self.ac_d2h, self.h2d_stream, config.ac_offload_dir)
+        trace = config.trace_path or os.environ.get("T1_TRACE") or None
+        if trace and self.world_size > 1:
+            trace = f"{trace}.rank{self.rank}"
+        self.tracer = PhaseTracer(self.device, trace, self.rank, self.world_size)
         self.completed_steps = 0
         self.stats: Dict[str, float] = {}
         self.h2d_bytes = 0
@@ -452,9 +457,13 @@ class SlideFSDP(nn.Module):
         st.unit = unit
         if need_weights:
             # the previous step's optimizer update of this layer must be visible
+            t0 = time.perf_counter()
             self.updates.wait_counter(st.idx, self._update_target(st))
+            self.tracer.host("wait_update", st.idx, time.perf_counter() - t0)
             self.h2d_stream.wait(unit.free_event)
+            tok = self.tracer.begin("h2d", st.idx, self.h2d_stream)
             self.comm.fetch_params(st, unit.param, self.h2d_stream)
+            self.tracer.end(tok)
             self.h2d_bytes += st.numel * unit.param.element_size()
             st.loaded = self.h2d_stream.record()
         else:
@@ -490,7 +499,9 @@ class SlideFSDP(nn.Module):
         computed = Event(self.device).record()
         self.grad_stream.wait(computed)
         unit = st.unit
+        tok = self.tracer.begin("grad_sync", st.idx, self.grad_stream)
         self.comm.sync_grads(st, unit.grad, self.grad_stream)
+        self.tracer.end(tok)
         ready = self.grad_stream.record()
         self._release(st, ready)
         self._schedule_update(st, ready, step)
@@ -506,7 +517,9 @@ class SlideFSDP(nn.Module):
         def run_update(grad=None):
             if has_work:
                 g = grad if grad is not None else st.grad_host
+                t0 = time.perf_counter()
                 opt.step_flat(st.idx, g, shadow=shadow, grad_scale=scale)
+                self.tracer.host("adam", st.idx, time.perf_counter() - t0)
             if e > s:  # only ranks that own a slice publish
                 self.updates.publish(st.idx)
 
@@ -558,7 +571,8 @@ class SlideFSDP(nn.Module):
         if L > 0 and not fuse_first:
             self._fetch(S[1], with_grad=False)
         self._wait_loaded(emb)
-        h = emb.module.forward_ids(ctx.input_ids)
+        with self.tracer.span("fwd", 0):
+            h = emb.module.forward_ids(ctx.input_ids)
         self._release(emb, Event(dev).record())
         prefetch = max(1, min(self.config.prefetch_layers, self.config.gpu_buffer_pool_size - 1))
         fuse_qkv = fuse_first
@@ -577,11 +591,13 @@ class SlideFSDP(nn.Module):
                     self._wait_loaded(st)
             else:
                 self._wait_loaded(st)
+            tok = self.tracer.begin("fwd", i)
             if self.config.enable_activation_checkpoint:
                 self.acts.save(i, h, keep_on_gpu=(i == L))
                 h, _ = st.module.forward_train(h, ctx, save=False, qkv_fn=qkv_fn)
             else:
                 h, saved_all[i] = st.module.forward_train(h, ctx, save=True, qkv_fn=qkv_fn)
+            self.tracer.end(tok)
             if not fuse_qkv:
                 # prefetch the next layer(s) into free units
                 for j in range(i + 1, min(i + prefetch, L) + 1):
@@ -598,7 +614,8 @@ class SlideFSDP(nn.Module):
 
         # ---------------- output layer: loss + its backward
         self._wait_loaded(out)
-        loss, dh = out.module.loss_and_grad(h, ctx)
+        with self.tracer.span("loss", L + 1):
+            loss, dh = out.module.loss_and_grad(h, ctx)
         del h
         if L > 0:
             S[L].bind_device(with_grad=True)
@@ -612,6 +629,7 @@ class SlideFSDP(nn.Module):
                 if self.config.enable_activation_checkpoint:
                     self.acts.prefetch(i - 1)
             self._wait_loaded(st)
+            tok = self.tracer.begin("bwd", i)
             if self.config.enable_activation_checkpoint:
                 h_in = self.acts.get(i)
                 _, saved = st.module.forward_train(h_in, ctx, save=True)
@@ -620,16 +638,20 @@ class SlideFSDP(nn.Module):
                 saved = saved_all.pop(i)
             dh = st.module.backward(saved, dh, ctx)
             del saved
+            self.tracer.end(tok)
             self._offload_grads(st, step)
 
         # ---------------- embedding backward (weights not needed)
         self._fetch(emb, with_grad=True, need_weights=False)
         self._wait_loaded(emb)
-        emb.module.backward_ids(dh, ctx.input_ids)
+        with self.tracer.span("bwd", 0):
+            emb.module.backward_ids(dh, ctx.input_ids)
         del dh
         self._offload_grads(emb, step)
         self.acts.clear()
         self.completed_steps = step
+        if self.tracer.enabled:
+            self.tracer.step_done(step, {"h2d_bytes": self.h2d_bytes})
         return loss
 
     @torch.no_grad()
