@@ -20,7 +20,12 @@ Extra fields (all optional, reference configs never set them):
         exact; the high plane doubles as the bf16 copy the GPUs load, so the
         optimizer writes no separate shadow: 2 fewer bytes of host memory
         traffic per parameter and step), "fp32" keeps plain fp32 plus a bf16
-        shadow.  Only bf16 training uses "split".
+        shadow.  Only bf16 training uses "split".  "bf16" keeps bf16 weights
+        only (each update rounded to nearest even), the reference's
+        bf16-parameter LayerAdam mode for models whose fp32 master does not
+        fit in host RAM.
+    optimizer_state_dtype: dtype of LayerAdam's m and v in host memory
+        ("fp32", or "bf16" to halve the state of very large models).
     host_wait_timeout_s: bound on every host-side wait for another rank
         (optimizer publication, cpu_reduce slots); expiry raises TimeoutError.
     trace_path: append one JSON line per training step with per-phase
@@ -91,7 +96,8 @@ class SlideFSDPConfig:
     shard_source: str = "master"  # shard fetch reads the fp32 "master" (cast on GPU) or the bf16 "shadow"
     host_threads: int = 0
     host_wait_timeout_s: float = 600.0  # bound on every host wait for a peer rank
-    master_layout: str = "split"  # "split" (hi/lo 16-bit planes) or "fp32" (plain fp32 + bf16 shadow)
+    master_layout: str = "split"  # "split" (hi/lo 16-bit planes), "fp32" (fp32 + bf16 shadow) or "bf16"
+    optimizer_state_dtype: str = "fp32"  # LayerAdam m/v in host memory: "fp32" or "bf16"
     use_native_kernels: Optional[bool] = None  # None: native iff device is CUDA
     trace_path: Optional[str] = None  # per-phase step trace (JSON lines); env T1_TRACE also enables it
 
@@ -119,8 +125,10 @@ class SlideFSDPConfig:
             raise ValueError(
                 f"optimizer_sharding must be 'rank' or 'rank0', got {self.optimizer_sharding}"
             )
-        if self.master_layout not in ("split", "fp32"):
-            raise ValueError(f"master_layout must be 'split' or 'fp32', got {self.master_layout}")
+        if self.master_layout not in ("split", "fp32", "bf16"):
+            raise ValueError(f"master_layout must be 'split', 'fp32' or 'bf16', got {self.master_layout}")
+        if self.optimizer_state_dtype not in ("fp32", "bf16"):
+            raise ValueError(f"optimizer_state_dtype must be 'fp32' or 'bf16', got {self.optimizer_state_dtype}")
         if self.shard_source not in ("master", "shadow"):
             raise ValueError(f"shard_source must be 'master' or 'shadow', got {self.shard_source}")
         if self.gpu_buffer_pool_size < 2:

@@ -122,6 +122,7 @@ class LayerAdam:
         nvme_offload_fraction: float = 0.0,
         offload_dir: str = "/tmp/opt_offload",
         prefetch: bool = True,
+        state_dtype: Optional[torch.dtype] = None,
     ):
         if not 0.0 <= nvme_offload_fraction <= 1.0:
             raise ValueError("nvme_offload_fraction must be in [0, 1]")
@@ -136,6 +137,8 @@ class LayerAdam:
         self.param_groups: list = []
         self._groups: Dict[int, dict] = {}
         self.fp32_optimizer_state = fp32_optimizer_state
+        # explicit m/v dtype of flat layers (overrides fp32_optimizer_state)
+        self.state_dtype = state_dtype
         self.num_layer = num_layer
         self.state: DefaultDict[torch.Tensor, Any] = defaultdict(dict)
         self.exp_avg_flat: "OrderedDict[int, torch.Tensor]" = OrderedDict()
@@ -194,7 +197,10 @@ class LayerAdam:
             raise ValueError("split master needs two planes of equal size")
         self._new_group(layer_idx, [])
         n = ts[0].numel()
-        sdt = torch.float32 if (planes or self.fp32_optimizer_state) else ts[0].dtype
+        if self.state_dtype is not None:
+            sdt = self.state_dtype
+        else:
+            sdt = torch.float32 if (planes or self.fp32_optimizer_state) else ts[0].dtype
         self.exp_avg_flat[layer_idx] = torch.zeros(n, dtype=sdt)
         self.exp_avg_sq_flat[layer_idx] = torch.zeros(n, dtype=sdt)
         self._flat_param[layer_idx] = tuple(ts) if planes else flat_param

@@ -174,7 +174,8 @@ class FusedComm(CollectiveComm):
         if self.shard_source == "master" and store is not None:
             if store.split:
                 return store.hi[s:e], store.lo[s:e]
-            return store.f32[s:e], None
+            if store.f32 is not None:
+                return store.f32[s:e], None
         return st.shadow[s:e], None
 
     def check(self) -> None:

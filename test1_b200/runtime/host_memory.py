@@ -131,42 +131,59 @@ class RegionPlanner:
 
 
 class MasterStore:
-    """One layer's fp32 master in host memory, stored either as plain fp32
-    plus a separate bf16 shadow, or "split": a bf16 high plane (which *is*
-    the shadow) followed by a 16-bit low plane (see host_kernels.h, kSplit).
+    """One layer's master weights in host memory.  Layouts:
+
+    * ``split`` -- fp32 stored as a bf16 high plane (which *is* the shadow the
+      GPUs load) followed by a 16-bit low plane (see host_kernels.h, kSplit);
+    * ``fp32``  -- plain fp32 plus a separate low-precision shadow;
+    * ``bf16``  -- bf16 only (the optimizer rounds every update to nearest
+      even): the reference's bf16-parameter LayerAdam mode, for models whose
+      fp32 master does not fit in host RAM (e.g. 70B on one node).
+
     All fp32 reads and writes go through this class."""
 
     def __init__(self, region: "HostRegion", numel: int, master_off: int, split: bool,
-                 shadow_dtype: torch.dtype, shadow_off: Optional[int] = None):
+                 shadow_dtype: torch.dtype, shadow_off: Optional[int] = None, layout: Optional[str] = None):
         self.numel = numel
-        self.split = split
-        if split:
+        self.layout = layout or ("split" if split else "fp32")
+        self.split = self.layout == "split"
+        self.lo = None
+        if self.layout == "split":
             self.hi = region.view(torch.bfloat16, master_off, numel)
             self.lo = region.view(torch.int16, master_off + 2 * numel, numel)
             self.f32 = None
             self.shadow = self.hi
+        elif self.layout == "bf16":
+            self.hi = region.view(torch.bfloat16, master_off, numel)
+            self.f32 = None
+            self.shadow = self.hi
         else:
             self.f32 = region.view(torch.float32, master_off, numel)
-            self.hi = self.lo = None
+            self.hi = None
             if shadow_dtype == torch.float32 or shadow_off is None:
                 self.shadow = self.f32
             else:
                 self.shadow = region.view(shadow_dtype, shadow_off, numel)
 
     @staticmethod
-    def bytes_needed(numel: int, split: bool, shadow: bool) -> tuple:
+    def bytes_needed(numel: int, split: bool, shadow: bool, layout: Optional[str] = None) -> tuple:
         """(master bytes, shadow bytes) to plan for one layer."""
-        return 4 * numel, (0 if split or not shadow else 2 * numel)
+        layout = layout or ("split" if split else "fp32")
+        if layout == "bf16":
+            return 2 * numel, 0
+        return 4 * numel, (0 if layout == "split" or not shadow else 2 * numel)
 
     @property
     def bind_tensor(self) -> torch.Tensor:
         """Flat tensor the offloaded module parameters point into."""
-        return self.hi if self.split else self.f32
+        return self.hi if self.f32 is None else self.f32
 
     def read_fp32(self, s: int = 0, e: Optional[int] = None, out: Optional[torch.Tensor] = None):
         e = self.numel if e is None else e
-        if not self.split:
+        if self.layout == "fp32":
             return self.f32[s:e] if out is None else out.copy_(self.f32[s:e])
+        if self.layout == "bf16":
+            return self.hi[s:e].float() if out is None else out.copy_(self.hi[s:e])
         out = torch.empty(e - s, dtype=torch.float32) if out is None else out
         _native.host().split_to_f32(self.hi[s:e], self.lo[s:e], out)
         return out
@@ -174,12 +191,16 @@ class MasterStore:
     def write_fp32(self, src: torch.Tensor, s: int = 0) -> None:
         e = s + src.numel()
         src = src.reshape(-1).float().contiguous()
-        if self.split:
+        if self.layout == "split":
             _native.host().f32_to_split(src, self.hi[s:e], self.lo[s:e])
+        elif self.layout == "bf16":
+            _native.host().cast_(self.hi[s:e], src, 1.0)
         else:
             self.f32[s:e].copy_(src)
             if self.shadow is not self.f32:
                 _native.host().cast_(self.shadow[s:e], self.f32[s:e], 1.0)
 
     def optim_slice(self, s: int, e: int):
-        return (self.hi[s:e], self.lo[s:e]) if self.split else self.f32[s:e]
+        if self.layout == "split":
+            return self.hi[s:e], self.lo[s:e]
+        return self.hi[s:e] if self.layout == "bf16" else self.f32[s:e]

@@ -170,11 +170,16 @@ class SlideFSDP(nn.Module):
         n_counters = 4 * self.num_layers + 64
         self._ctr_off = plan.take(8 * n_counters)
         self.split_master = self.dtype == torch.bfloat16 and config.master_layout == "split"
+        if self.dtype == torch.bfloat16 and config.master_layout == "bf16":
+            self.master_layout = "bf16"
+        else:
+            self.master_layout = "split" if self.split_master else "fp32"
         want_shadow = self.dtype != torch.float32
         for l in self.layouts:
-            l.master_off = plan.take(4 * l.numel)
+            mb, _ = MasterStore.bytes_needed(l.numel, self.split_master, want_shadow, self.master_layout)
+            l.master_off = plan.take(mb)
         for l in self.layouts:
-            _, sb = MasterStore.bytes_needed(l.numel, self.split_master, want_shadow)
+            _, sb = MasterStore.bytes_needed(l.numel, self.split_master, want_shadow, self.master_layout)
             l.shadow_off = plan.take(sb) if sb else None
         dec_caps = [l.numel for l in self.layouts if l.kind == "decoder"]
         big_caps = [l.numel for l in self.layouts if l.kind != "decoder"]
@@ -210,7 +215,7 @@ class SlideFSDP(nn.Module):
 
         # ---- master stores; init (rank 0 writes), then everyone pins
         self.stores = [MasterStore(self.shared, l.numel, l.master_off, self.split_master, self.dtype,
-                                   l.shadow_off) for l in self.layouts]
+                                   l.shadow_off, layout=self.master_layout) for l in self.layouts]
         self._init_master(model)
         if self.world_size > 1:
             dist.barrier()
@@ -375,7 +380,8 @@ class SlideFSDP(nn.Module):
                         weight_decay=config.weight_decay, bias_correction=config.bias_correction,
                         adamw_mode=True, fp32_optimizer_state=True, num_layer=self.num_layers,
                         nvme_offload_fraction=config.optimizer_nvme_offload_fraction,
-                        offload_dir=config.optimizer_offload_dir, prefetch=True)
+                        offload_dir=config.optimizer_offload_dir, prefetch=True,
+                        state_dtype=torch.bfloat16 if config.optimizer_state_dtype == "bf16" else None)
         n = 0
         for st in self.layer_states:
             s, e = st.shard
@@ -511,7 +517,7 @@ class SlideFSDP(nn.Module):
         s, e = st.shard
         has_work = opt is not None and e > s
         scale = self.comm.grad_scale
-        shadow = (st.shadow[s:e] if (has_work and self.dtype != torch.float32 and not st.store.split)
+        shadow = (st.shadow[s:e] if (has_work and st.store.layout == "fp32" and self.dtype != torch.float32)
                   else None)
 
         def run_update(grad=None):

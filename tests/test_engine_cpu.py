@@ -115,3 +115,33 @@ def test_split_master_matches_fp32_master_bf16():
         # bounds each element's drift by 2 lr per step
         assert (d > 1e-4).float().mean().item() < 0.1, n
         assert d.max().item() <= 3 * 2 * 1e-3 + 1e-5, n
+
+
+def test_bf16_master_and_bf16_state_train():
+    """The large-model mode (bf16 weights and bf16 Adam state in host
+    memory): the stores are bf16 only and training tracks the fp32-master
+    run closely over a few steps."""
+    cfg = LlamaConfig.tiny()
+    runs = {}
+    for layout, sdt in (("bf16", "bf16"), ("split", "fp32")):
+        torch.manual_seed(0)
+        eng = SlideFSDP(LlamaForCausalLM(cfg), SlideFSDPConfig(dtype=torch.bfloat16, device="cpu", lr=1e-3,
+                                                              master_layout=layout, optimizer_state_dtype=sdt))
+        g = torch.Generator().manual_seed(5)
+        try:
+            if layout == "bf16":
+                st = eng.layer_states[1]
+                assert st.store.f32 is None and st.store.lo is None
+                assert eng.layer_optimizer.exp_avg_flat[1].dtype == torch.bfloat16
+            losses = []
+            for _ in range(4):
+                ids = torch.randint(0, cfg.vocab_size, (2, 32), generator=g)
+                losses.append(float(eng(input_ids=ids, labels=ids).loss))
+            eng.wait_for_updates()
+            runs[layout] = losses
+        finally:
+            eng.close()
+    a, b = runs["bf16"], runs["split"]
+    assert abs(a[0] - b[0]) < 1e-3
+    for x, y in zip(a, b):
+        assert abs(x - y) < 5e-2
