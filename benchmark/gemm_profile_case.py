@@ -1,6 +1,6 @@
 """One GEMM shape, a few launches: the small case for an ncu capture of the
 tcgen05 GEMM (Llama-3.1-8B QKV projection: 4096 x 6144 x 4096, ~130 MB of
-operands).  Usage: python benchmark/gemm_profile_case.py [fwd|dgrad|wgrad]"""
+operands).  Usage: python benchmark/gemm_profile_case.py [fwd|dgrad|wgrad] [--pair]"""
 import os
 import sys
 
@@ -10,6 +10,8 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from test1_b200.ops import native  # noqa: E402
 
 kind = sys.argv[1] if len(sys.argv) > 1 else "fwd"
+if "--pair" in sys.argv:
+    native.gemm_set_mode(1)
 M, N, K = 4096, 6144, 4096
 x = torch.randn(M, K, device="cuda").bfloat16()
 w = torch.randn(N, K, device="cuda").bfloat16()

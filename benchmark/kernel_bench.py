@@ -41,7 +41,7 @@ def peaks():
         return 1590.0, 6650.0, "of fallback"
 
 
-def bench_gemm(T=4096, H=4096, I=14336, nq=32, nkv=8, D=128):
+def bench_gemm(T=4096, H=4096, I=14336, nq=32, nkv=8, D=128, modes=(0, 1)):
     tf_peak, _, tag = peaks()
     out = []
     shapes = {
@@ -55,19 +55,22 @@ def bench_gemm(T=4096, H=4096, I=14336, nq=32, nkv=8, D=128):
         w = torch.randn(N, K, device="cuda").bfloat16()
         y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         fl = 2 * M * N * K
-        ours = timeit(lambda: native.gemm(x, w, y))
-        cub = timeit(lambda: torch.matmul(x, w.t(), out=y))
         dy = torch.randn(M, N, device="cuda").bfloat16()
         dx = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
-        dg = timeit(lambda: native.gemm(dy, w, dx, False, True))
-        dgc = timeit(lambda: torch.matmul(dy, w, out=dx))
         dw = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
-        wg = timeit(lambda: native.gemm(dy, x, dw, True, True))
+        cub = timeit(lambda: torch.matmul(x, w.t(), out=y))
+        dgc = timeit(lambda: torch.matmul(dy, w, out=dx))
         wgc = timeit(lambda: torch.matmul(dy.t(), x, out=dw))
-        for kind, t, tc in (("fwd", ours, cub), ("dgrad", dg, dgc), ("wgrad", wg, wgc)):
-            out.append({"kernel": f"gemm_{name}_{kind}", "M": M, "N": N, "K": K, "ms": round(t, 4),
-                        "tflops": round(fl / t / 1e9, 1), "frac_peak": round(fl / t / 1e9 / tf_peak, 3),
-                        "peak_ref": tag, "cublas_ms": round(tc, 4), "vs_cublas": round(tc / t, 3)})
+        for mode in modes:
+            native.gemm_set_mode(mode)
+            ours = timeit(lambda: native.gemm(x, w, y))
+            dg = timeit(lambda: native.gemm(dy, w, dx, False, True))
+            wg = timeit(lambda: native.gemm(dy, x, dw, True, True))
+            for kind, t, tc in (("fwd", ours, cub), ("dgrad", dg, dgc), ("wgrad", wg, wgc)):
+                out.append({"kernel": f"gemm_{name}_{kind}", "mode": "pair" if mode else "single",
+                            "M": M, "N": N, "K": K, "ms": round(t, 4),
+                            "tflops": round(fl / t / 1e9, 1), "frac_peak": round(fl / t / 1e9 / tf_peak, 3),
+                            "peak_ref": tag, "cublas_ms": round(tc, 4), "vs_cublas": round(tc / t, 3)})
     return out
 
 

@@ -23,6 +23,8 @@ std::vector<torch::Tensor> cross_entropy_fwd_bwd(torch::Tensor logits, torch::Te
 void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, bool b_mn,
                c10::optional<torch::Tensor> R);
 int64_t gemm_check_error(bool reset);
+void gemm_set_mode(int64_t mode);
+int64_t gemm_get_mode();
 std::vector<torch::Tensor> attention_fwd(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                          int64_t S);
 torch::Tensor attention_bwd(torch::Tensor dout, torch::Tensor qkv, torch::Tensor out,
@@ -58,6 +60,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &t1::gemm_bf16, pybind11::arg("A"), pybind11::arg("B"), pybind11::arg("C"),
         pybind11::arg("a_mn"), pybind11::arg("b_mn"), pybind11::arg("R") = pybind11::none());
   m.def("gemm_check_error", &t1::gemm_check_error, pybind11::arg("reset") = false);
+  m.def("gemm_set_mode", &t1::gemm_set_mode, "0: single-CTA tiles, 1: CTA-pair (cta_group::2) tiles");
+  m.def("gemm_get_mode", &t1::gemm_get_mode);
   m.def("attention_fwd", &t1::attention_fwd);
   m.def("attention_bwd", &t1::attention_bwd);
   m.def("fused_rs_d2h", &t1::fused_rs_d2h);

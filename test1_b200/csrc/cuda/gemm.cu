@@ -26,7 +26,15 @@
 // Tiles are visited in grouped (GROUP_M) raster order for L2 reuse.  All
 // barrier waits are bounded (see sm100.cuh); a timeout writes a code to the
 // error word and the CTA unwinds.
+//
+// Pair mode (gemm_pair.cuh, cta_group::2): CTA pairs compute 256 x 256
+// tiles with one MMA stream, each CTA staging half of the operands.  The
+// mode is chosen per process: gemm_set_mode(0 = single CTA, 1 = pairs), or
+// the environment variable T1_GEMM_PAIR.
 #include "gemm_core.cuh"
+#include "gemm_pair.cuh"
+
+#include <cstdlib>
 
 namespace t1 {
 
@@ -82,8 +90,39 @@ torch::Tensor& gemm_error_word() {
   return it->second;
 }
 
+static int& gemm_mode() {
+  static int mode = [] {
+    const char* e = std::getenv("T1_GEMM_PAIR");
+    return (e != nullptr && e[0] == '1') ? 1 : 0;
+  }();
+  return mode;
+}
+
+void gemm_set_mode(int64_t mode) {
+  TORCH_CHECK(mode == 0 || mode == 1, "GEMM mode must be 0 (single CTA) or 1 (CTA pairs)");
+  gemm_mode() = static_cast<int>(mode);
+}
+
+int64_t gemm_get_mode() { return gemm_mode(); }
+
+template <bool A_MN, bool B_MN, int EPI>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p) {
+  auto kern = gemm::gemm_pair_kernel<A_MN, B_MN, EPI>;
+  static bool configured = false;
+  if (!configured) {
+    T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       gemm::PAIR_SMEM_BYTES));
+    configured = true;
+  }
+  const int clusters = std::min(p.num_tiles, num_sms() / 2);
+  kern<<<2 * clusters, 192, gemm::PAIR_SMEM_BYTES, stream()>>>(ta, tb, p);
+  check_launch("gemm_bf16 (pair)");
+  count_launch();
+}
+
 template <bool A_MN, bool B_MN, int EPI>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p) {
+  if (gemm_mode() == 1) return launch_pair<A_MN, B_MN, EPI>(ta, tb, p);
   auto kern = gemm::gemm_bf16_kernel<A_MN, B_MN, EPI, false>;
   static bool configured = false;
   if (!configured) {
@@ -121,10 +160,13 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, boo
     else C.zero_();
     return;
   }
+  const bool pair = gemm_mode() == 1;
   CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), 64)
-                        : make_map(A.data_ptr(), K, M, A.stride(0), gemm::BM);
+                        : make_map(A.data_ptr(), K, M, A.stride(0), pair ? gemm::PAIR_HALF : gemm::BM);
   CUtensorMap tb = b_mn ? make_map(B.data_ptr(), N, K, B.stride(0), 64)
-                        : make_map(B.data_ptr(), K, N, B.stride(0), gemm::BN);
+                        : make_map(B.data_ptr(), K, N, B.stride(0), pair ? gemm::PAIR_HALF : gemm::BN);
+  const int tile_m = pair ? gemm::PAIR_BM : gemm::BM;
+  const int tile_n = pair ? gemm::PAIR_BN : gemm::BN;
   gemm::Params p;
   p.M = M;
   p.N = N;
@@ -133,8 +175,8 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, boo
   p.ldc = C.stride(0);
   p.R = nullptr;
   p.ldr = 0;
-  p.tiles_m = (M + gemm::BM - 1) / gemm::BM;
-  p.tiles_n = (N + gemm::BN - 1) / gemm::BN;
+  p.tiles_m = (M + tile_m - 1) / tile_m;
+  p.tiles_n = (N + tile_n - 1) / tile_n;
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_blocks = (K + gemm::BK - 1) / gemm::BK;
   p.err = gemm_error_word().data_ptr<int>();

@@ -358,12 +358,18 @@ __global__ void __launch_bounds__(AG ? 256 : 192, 1)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (*abort_flag) break;
-      if (!mbar_wait(&tfull[acc], acc_phase)) {
-        err.set(104);
-        *abort_flag = 1;
-        break;
+      // one lane waits and the warp follows it, so the warp never diverges
+      // around the .sync.aligned TMEM loads below
+      int ok = 0;
+      if (lane == 0) {
+        ok = !*abort_flag;
+        if (ok && !mbar_wait(&tfull[acc], acc_phase)) {
+          err.set(104);
+          *abort_flag = 1;
+          ok = 0;
+        }
       }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       tc_fence_after();
       int mb, nb;
       raster(tile, p.tiles_m, p.tiles_n, mb, nb);

@@ -1,0 +1,236 @@
+// tcgen05 GEMM on CTA pairs (cta_group::2): the pair computes a 256 x 256
+// tile with one MMA stream issued by the even ("leader") CTA.  Each CTA
+// stages only its own half of the tile's operands (128 rows of A and 128
+// rows of B per k-block: 32 KB instead of the 48 KB a single CTA needs for
+// 128 x 256), so shared-memory fill traffic from L2 per FLOP drops by a
+// third -- the single-CTA kernel (gemm_core.cuh) is bound by exactly that
+// traffic.  Accumulators: 256 x 256 fp32 split over both CTAs' TMEM (each
+// holds its 128 rows), double-buffered (2 x 256 columns).
+//
+// Pair protocol (all waits bounded, see sm100.cuh):
+//   full[s]    leader's barrier; the leader arms it with both CTAs' bytes,
+//              both CTAs' TMA loads count on it (.cta_group::2 form)
+//   empty[s]   per CTA; the leader's MMA commit arrives on both (mask 0b11)
+//   tfull[a]   per CTA; accumulator a finished (commit to both)
+//   tempty[a]  leader's; the 4 epilogue warps of each CTA arrive (count 8)
+// No TMA load uses multicast.
+#pragma once
+
+#include "gemm_core.cuh"
+
+namespace t1 {
+namespace gemm {
+
+constexpr int PAIR_BM = 256;
+constexpr int PAIR_BN = 256;
+constexpr int PAIR_HALF = 128;
+constexpr int PAIR_STAGES = 6;
+constexpr int PAIR_A_BYTES = PAIR_HALF * BK * 2;
+constexpr int PAIR_B_BYTES = PAIR_HALF * BK * 2;
+constexpr int PAIR_STAGE_BYTES = PAIR_A_BYTES + PAIR_B_BYTES;
+constexpr int PAIR_SMEM_BYTES = PAIR_STAGES * PAIR_STAGE_BYTES + 1024 + 256;
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
+                     const __grid_constant__ CUtensorMap tma_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + PAIR_STAGES * PAIR_A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + PAIR_STAGES * PAIR_B_BYTES);
+  uint64_t* empty = full + PAIR_STAGES;
+  uint64_t* tfull = empty + PAIR_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();  // 0 = leader
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+  const ErrorSlot err{p.err};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PAIR_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tma_a);
+    prefetch_tensormap(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = cluster; tile < p.num_tiles && !*abort_flag; tile += nclusters) {
+        int mb, nb;
+        raster(tile, p.tiles_m, p.tiles_n, mb, nb);
+        const int row_a = mb * PAIR_BM + static_cast<int>(crank) * PAIR_HALF;
+        const int row_b = nb * PAIR_BN + static_cast<int>(crank) * PAIR_HALF;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            err.set(111);
+            *abort_flag = 1;
+            break;
+          }
+          const uint32_t lfull = mapa_shared(smem_u32(&full[stage]), 0);
+          if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * PAIR_STAGE_BYTES);
+          uint8_t* a = sA + stage * PAIR_A_BYTES;
+          uint8_t* b = sB + stage * PAIR_B_BYTES;
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d_pair(a, &tma_a, lfull, k0, row_a);
+          } else {
+            tma_load_2d_pair(a, &tma_a, lfull, row_a, k0);
+            tma_load_2d_pair(a + 8192, &tma_a, lfull, row_a + 64, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(b, &tma_b, lfull, k0, row_b);
+          } else {
+            tma_load_2d_pair(b, &tma_b, lfull, row_b, k0);
+            tma_load_2d_pair(b + 8192, &tma_b, lfull, row_b + 64, k0);
+          }
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------- MMA issuer (leader only)
+    if (lane == 0 && crank == 0) {
+      constexpr uint32_t IDESC = idesc_bf16_f32(PAIR_BM, PAIR_BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = cluster; tile < p.num_tiles && !*abort_flag; tile += nclusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
+          err.set(112);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * PAIR_BN;
+        bool ok = true;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) {
+            err.set(113);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * PAIR_A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * PAIR_B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? smem_desc_sw128(a_addr + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + k * 2048, 8192, 1024)
+                                     : smem_desc_sw128(b_addr + k * 32, 16, 1024);
+            mma_bf16_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == PAIR_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(&tfull[acc], 0x3);
+      }
+    }
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t leader_tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint32_t leader_tempty1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    int local = 0;
+    for (int tile = cluster; tile < p.num_tiles; tile += nclusters, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      // one lane waits and the warp follows it, so the warp never diverges
+      // around the .sync.aligned TMEM loads below
+      int ok = 0;
+      if (lane == 0) {
+        ok = !*abort_flag;
+        if (ok && !mbar_wait(&tfull[acc], acc_phase)) {
+          err.set(114);
+          *abort_flag = 1;
+          ok = 0;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      tc_fence_after();
+      int mb, nb;
+      raster(tile, p.tiles_m, p.tiles_n, mb, nb);
+      const int row = mb * PAIR_BM + static_cast<int>(crank) * PAIR_HALF + q * 32 + lane;
+      const bool row_ok = row < p.M;
+      bf16* crow = p.C + static_cast<long>(row) * p.ldc;
+#pragma unroll 1
+      for (int c = 0; c < PAIR_BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * PAIR_BN + c, r);
+        tmem_ld_wait();
+        const int col0 = nb * PAIR_BN + c;
+        if (row_ok) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int col = col0 + 8 * v;
+            if (col < p.N) {
+              float f[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);
+              if (EPI == kAddResidual) {
+                float rv[8];
+                load8(p.R + static_cast<long>(row) * p.ldr + col, rv);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) f[j] += rv[j];
+              }
+              store8(crow + col, f);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // neither CTA leaves while the pair still uses its smem / TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace gemm
+}  // namespace t1

@@ -62,6 +62,15 @@ def gemm(a, b, c, a_mn=False, b_mn=False, residual=None):
     return c
 
 
+def gemm_set_mode(mode: int) -> None:
+    """0: single-CTA 128x256 tiles; 1: CTA-pair (cta_group::2) 256x256 tiles."""
+    _c().gemm_set_mode(int(mode))
+
+
+def gemm_get_mode() -> int:
+    return int(_c().gemm_get_mode())
+
+
 def gemm_error(reset: bool = False) -> int:
     return int(_c().gemm_check_error(reset))
 

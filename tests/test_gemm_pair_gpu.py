@@ -1,0 +1,65 @@
+"""CTA-pair (cta_group::2) GEMM vs an fp32 PyTorch product, in all three
+operand layouts and with the residual epilogue, at shapes with ragged M, N
+and K edges; also checks that the pair path leaves no error code."""
+import pytest
+import torch
+
+from test1_b200 import _native
+from test1_b200.ops import native
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(256, 256, 64), (300, 264, 200), (1000, 776, 1536), (4096, 6144, 4096), (130, 1024, 4096)]
+
+
+def _rel(a, b):
+    return ((a.float() - b).norm() / b.norm().clamp_min(1e-6)).item()
+
+
+@pytest.fixture
+def pair_mode():
+    C = _native.cuda()
+    old = C.gemm_get_mode()
+    C.gemm_set_mode(1)
+    C.gemm_check_error(True)
+    yield C
+    torch.cuda.synchronize()
+    code = C.gemm_check_error(True)
+    C.gemm_set_mode(old)
+    assert code == 0, f"pair GEMM reported error code {code}"
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_pair_forward(pair_mode, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    assert _rel(native.linear_fwd(x, w), x.float() @ w.float().t()) < 6e-3
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES[:3])
+def test_pair_residual(pair_mode, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    r = torch.randn(M, N, device="cuda", generator=g).bfloat16() * 10
+    y = native.linear_fwd(x, w, residual=r)
+    assert _rel(y, x.float() @ w.float().t() + r.float()) < 6e-3
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_pair_dgrad(pair_mode, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(5)
+    dy = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    assert _rel(native.linear_dgrad(dy, w), dy.float() @ w.float()) < 6e-3
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_pair_wgrad(pair_mode, M, N, K):
+    g = torch.Generator(device="cuda").manual_seed(9)
+    dy = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    out = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
+    native.linear_wgrad(dy, x, out=out)
+    assert _rel(out, dy.float().t() @ x.float()) < 6e-3
