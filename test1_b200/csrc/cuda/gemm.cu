@@ -30,7 +30,7 @@
 // Pair mode (gemm_pair.cuh, cta_group::2): CTA pairs compute 256 x 256
 // tiles with one MMA stream, each CTA staging half of the operands.  The
 // mode is chosen per process: gemm_set_mode(0 = single CTA, 1 = pairs), or
-// the environment variable T1_GEMM_PAIR.
+// the environment variable T1_GEMM_PAIR (default: pairs).
 #include "gemm_core.cuh"
 #include "gemm_pair.cuh"
 
@@ -93,7 +93,7 @@ torch::Tensor& gemm_error_word() {
 static int& gemm_mode() {
   static int mode = [] {
     const char* e = std::getenv("T1_GEMM_PAIR");
-    return (e != nullptr && e[0] == '1') ? 1 : 0;
+    return (e != nullptr && e[0] == '0') ? 0 : 1;  // pairs unless T1_GEMM_PAIR=0
   }();
   return mode;
 }

@@ -45,7 +45,9 @@ def test_multi_tensor_adam_matches_reference(dtype, mode):
     noop = torch.zeros(1, dtype=torch.int32, device=dev)
     multi_tensor_adam(1000, noop, lists, 1e-3, 0.9, 0.999, 1e-8, 3, mode, 1, 0.01)
     torch.cuda.synchronize()
-    tol = {torch.float32: 1e-6, torch.float64: 1e-6, torch.bfloat16: 1e-2, torch.float16: 2e-3}[dtype]
+    # fp32 arithmetic in the kernel (also for fp64 tensors, as in the
+    # reference's functor): a few ulps against the float64 statement
+    tol = {torch.float32: 1e-5, torch.float64: 1e-5, torch.bfloat16: 1e-2, torch.float16: 2e-3}[dtype]
     for (rp, rm, rv), p, m, v in zip(refs, lists[1], lists[2], lists[3]):
         for got, want in ((p, rp), (m, rm), (v, rv)):
             err = (got.double() - want).abs() / (want.abs() + 1e-3)

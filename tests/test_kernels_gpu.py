@@ -160,3 +160,26 @@ def test_attention_fwd_bwd(B, S, nq, nkv):
     assert _rel(dqkv[:, :nqd], dqkve[:, :nqd]) < 2e-2, "dq"
     assert _rel(dqkv[:, nqd:nqd + nkd], dqkve[:, nqd:nqd + nkd]) < 2e-2, "dk"
     assert _rel(dqkv[:, nqd + nkd:], dqkve[:, nqd + nkd:]) < 2e-2, "dv"
+
+
+@pytest.mark.parametrize("B,S,hq,hkv", [(2, 1024, 4, 2), (1, 192, 2, 1), (2, 320, 8, 2)])
+def test_attention_tcgen05_forward_matches_reference(B, S, hq, hkv):
+    """tcgen05 forward (TMEM accumulators, P through shared memory) vs the
+    fp32 statement, and against the mma.sync forward's outputs."""
+    D = 128
+    torch.manual_seed(B * S + hq)
+    qkv = (torch.randn(B * S, (hq + 2 * hkv) * D, device="cuda") * 0.5).bfloat16()
+    old = native.attn_get_mode()
+    try:
+        native.attn_set_mode(1)
+        o, lse = native.attention_qkv_fwd(qkv, hq, hkv, D, S)
+        native.attn_set_mode(0)
+        o0, lse0 = native.attention_qkv_fwd(qkv, hq, hkv, D, S)
+    finally:
+        native.attn_set_mode(old)
+    torch.cuda.synchronize()
+    oe, lsee = ref.attention_qkv_fwd(qkv.float(), hq, hkv, D, S)
+    assert _rel(o, oe) < 1e-2
+    assert torch.allclose(lse, lsee, atol=2e-3, rtol=1e-3)
+    assert _rel(o, o0) < 1e-2
+    assert torch.allclose(lse, lse0, atol=2e-3, rtol=1e-3)
