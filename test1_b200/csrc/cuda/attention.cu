@@ -13,6 +13,8 @@
 // included); backward writes dq/dk/dv into dqkv [T, (Hq + 2 Hkv) * 128].
 #include "common.cuh"
 
+#include <cstdlib>
+
 namespace t1 {
 namespace attn {
 
@@ -470,8 +472,29 @@ static void check_qkv(const torch::Tensor& qkv, int64_t n_q, int64_t n_kv, int64
   TORCH_CHECK(qkv.stride(0) % 8 == 0, "qkv row stride must be a multiple of 8");
 }
 
+std::vector<torch::Tensor> attention_fwd_tc(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
+                                            int64_t S);
+
+// Forward implementation: 0 = mma.sync tiles (this file), 1 = tcgen05
+// (attention_tc.cu).  Per process: attn_set_mode() or T1_ATTN_TC=1.
+static int& attn_mode() {
+  static int mode = [] {
+    const char* e = std::getenv("T1_ATTN_TC");
+    return (e != nullptr && e[0] == '1') ? 1 : 0;
+  }();
+  return mode;
+}
+
+void attn_set_mode(int64_t mode) {
+  TORCH_CHECK(mode == 0 || mode == 1, "attention mode must be 0 (mma.sync) or 1 (tcgen05)");
+  attn_mode() = static_cast<int>(mode);
+}
+
+int64_t attn_get_mode() { return attn_mode(); }
+
 std::vector<torch::Tensor> attention_fwd(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                          int64_t S) {
+  if (attn_mode() == 1) return attention_fwd_tc(qkv, n_q, n_kv, D, S);
   check_qkv(qkv, n_q, n_kv, D, S);
   const int64_t T = qkv.size(0), B = T / S;
   auto out = torch::empty({T, n_q * D}, qkv.options());

@@ -27,6 +27,10 @@ void gemm_set_mode(int64_t mode);
 int64_t gemm_get_mode();
 std::vector<torch::Tensor> attention_fwd(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                          int64_t S);
+std::vector<torch::Tensor> attention_fwd_tc(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
+                                            int64_t S);
+void attn_set_mode(int64_t mode);
+int64_t attn_get_mode();
 torch::Tensor attention_bwd(torch::Tensor dout, torch::Tensor qkv, torch::Tensor out,
                             torch::Tensor lse, int64_t n_q, int64_t n_kv, int64_t D, int64_t S);
 void fused_rs_d2h(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t world,
@@ -64,6 +68,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_get_mode", &t1::gemm_get_mode);
   m.def("attention_fwd", &t1::attention_fwd);
   m.def("attention_bwd", &t1::attention_bwd);
+  m.def("attention_fwd_tc", &t1::attention_fwd_tc);
+  m.def("attn_set_mode", &t1::attn_set_mode, "0: mma.sync forward, 1: tcgen05 forward");
+  m.def("attn_get_mode", &t1::attn_get_mode);
   m.def("fused_rs_d2h", &t1::fused_rs_d2h);
   m.def("fused_shard_gather", &t1::fused_shard_gather);
   m.def("fused_ag_qkv", &t1::fused_ag_qkv);

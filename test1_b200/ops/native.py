@@ -71,6 +71,15 @@ def gemm_get_mode() -> int:
     return int(_c().gemm_get_mode())
 
 
+def attn_set_mode(mode: int) -> None:
+    """Attention forward: 0 = mma.sync tiles, 1 = tcgen05 (TMEM accumulators)."""
+    _c().attn_set_mode(int(mode))
+
+
+def attn_get_mode() -> int:
+    return int(_c().attn_get_mode())
+
+
 def gemm_error(reset: bool = False) -> int:
     return int(_c().gemm_check_error(reset))
 
