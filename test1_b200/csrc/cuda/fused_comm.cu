@@ -232,17 +232,22 @@ void fused_rs_d2h(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t 
                   int64_t offset, int64_t n, torch::Tensor host_out, double scale, int64_t epoch,
                   torch::Tensor counter, torch::Tensor err) {
   auto pe = make_peers(ptrs, sigs, world);
-  TORCH_CHECK(host_out.scalar_type() == torch::kBFloat16 && host_out.is_contiguous() &&
-                  host_out.numel() >= n, "host_out must be a contiguous bf16 tensor of >= n elements");
-  TORCH_CHECK(offset % 8 == 0, "shard offset must be a multiple of 8 elements");
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(host_out.data_ptr()) % 16 == 0, "host_out misaligned");
   TORCH_CHECK(counter.is_cuda() && err.is_cuda(), "counter/err must live on the GPU");
-  if (n <= 0) return;
-  void* out_dev = host_out.data_ptr();
-  if (host_out.device().is_cpu()) {
-    T1_CHECK_CUDA(cudaHostGetDevicePointer(&out_dev, host_out.data_ptr(), 0));
+  // A rank whose share of the range is empty still launches (one CTA): the
+  // launch is its half of the per-epoch handshake with the peers.
+  if (n < 0) n = 0;
+  void* out_dev = nullptr;
+  if (n > 0) {
+    TORCH_CHECK(host_out.scalar_type() == torch::kBFloat16 && host_out.is_contiguous() &&
+                    host_out.numel() >= n, "host_out must be a contiguous bf16 tensor of >= n elements");
+    TORCH_CHECK(offset % 8 == 0, "shard offset must be a multiple of 8 elements");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(host_out.data_ptr()) % 16 == 0, "host_out misaligned");
+    out_dev = host_out.data_ptr();
+    if (host_out.device().is_cpu()) {
+      T1_CHECK_CUDA(cudaHostGetDevicePointer(&out_dev, host_out.data_ptr(), 0));
+    }
   }
-  fused::rs_d2h_kernel<<<comm_grid(n / 8), 256, 0, stream()>>>(
+  fused::rs_d2h_kernel<<<n > 0 ? comm_grid(n / 8) : 1, 256, 0, stream()>>>(
       pe, rank, world, offset, n, reinterpret_cast<__nv_bfloat16*>(out_dev), (float)scale,
       static_cast<uint32_t>(epoch), counter.data_ptr<int>(), err.data_ptr<int>());
   check_launch("fused_rs_d2h");
@@ -264,6 +269,15 @@ void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, in
                         c10::optional<torch::Tensor> host_src_lo, int64_t epoch,
                         torch::Tensor counter, torch::Tensor err) {
   auto pe = make_peers(ptrs, sigs, world);
+  if (n <= 0) {
+    // empty share: still take part in the per-epoch handshake (one CTA)
+    fused::shard_gather_kernel<<<1, 256, 0, stream()>>>(pe, rank, world, offset, 0, fused::kSrcBf16,
+                                                        nullptr, nullptr, static_cast<uint32_t>(epoch),
+                                                        counter.data_ptr<int>(), err.data_ptr<int>());
+    check_launch("fused_shard_gather");
+    count_launch();
+    return;
+  }
   TORCH_CHECK(host_src.is_contiguous() && host_src.numel() >= n, "host_src too small");
   TORCH_CHECK(offset % 8 == 0, "shard offset must be a multiple of 8 elements");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(host_src.data_ptr()) % 16 == 0, "host_src misaligned");
@@ -282,7 +296,6 @@ void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, in
     TORCH_CHECK(host_src.scalar_type() == torch::kBFloat16, "host_src must be fp32 or bf16");
     kind = fused::kSrcBf16;
   }
-  if (n <= 0) return;
   fused::shard_gather_kernel<<<comm_grid(n / 8), 256, 0, stream()>>>(
       pe, rank, world, offset, n, kind, device_view(host_src), lo, static_cast<uint32_t>(epoch),
       counter.data_ptr<int>(), err.data_ptr<int>());

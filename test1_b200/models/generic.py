@@ -73,7 +73,7 @@ class GenericDecoderLayer(nn.Module):
     def forward(self, h, ctx):
         return self.forward_train(h, ctx, save=False)[0]
 
-    def backward(self, saved, dh: torch.Tensor, ctx) -> torch.Tensor:
+    def backward(self, saved, dh: torch.Tensor, ctx, grad_ready=None) -> torch.Tensor:
         h = saved.detach().requires_grad_(True)
         _zero_grads(self.layer)
         with torch.enable_grad():

@@ -277,28 +277,36 @@ class LlamaDecoderLayer(nn.Module):
     def forward(self, h: torch.Tensor, ctx: StepContext) -> torch.Tensor:
         return self.forward_train(h, ctx, save=False)[0]
 
-    def backward(self, saved, dh3: torch.Tensor, ctx: StepContext) -> torch.Tensor:
+    def backward(self, saved, dh3: torch.Tensor, ctx: StepContext, grad_ready=None) -> torch.Tensor:
+        """``grad_ready(t)``, when given, is called (on the compute stream's
+        timeline) with each weight gradient as soon as it is final: down,
+        gate/up, o, qkv; the norm gradients come last."""
         cfg = self.cfg
+        ready = grad_ready if grad_ready is not None else (lambda t: None)
         h, x1, rstd1, qkv, o, lse, h2, x2, rstd2, gu, a = saved
         Hq, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         w_qkv, w_o, w_gu, w_down = self._w()
         g_qkv, g_o, g_gu, g_down, g_ln1, g_ln2 = self._g()
         da = ops.linear_dgrad(dh3, w_down)
         ops.linear_wgrad(dh3, a, out=g_down)
+        ready(g_down)
         dgu = ops.swiglu_bwd(da, gu)
         del da
         dx2 = ops.linear_dgrad(dgu, w_gu)
         ops.linear_wgrad(dgu, x2, out=g_gu)
+        ready(g_gu)
         del dgu
         dh2, dw2 = ops.rmsnorm_bwd(dx2, h2, self.post_attention_layernorm.weight.data, rstd2, dh3)
         g_ln2.copy_(dw2)
         do = ops.linear_dgrad(dh2, w_o)
         ops.linear_wgrad(dh2, o, out=g_o)
+        ready(g_o)
         dqkv = ops.attention_bwd(do, qkv, o, lse, Hq, Hkv, D, ctx.seq_len)
         del do
         ops.rope_qkv_(dqkv, Hq, Hkv, D, ctx.cos, ctx.sin, ctx.seq_len, inverse=True)
         dx1 = ops.linear_dgrad(dqkv, w_qkv)
         ops.linear_wgrad(dqkv, x1, out=g_qkv)
+        ready(g_qkv)
         del dqkv
         dh, dw1 = ops.rmsnorm_bwd(dx1, h, self.input_layernorm.weight.data, rstd1, dh2)
         g_ln1.copy_(dw1)

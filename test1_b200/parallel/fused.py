@@ -139,6 +139,29 @@ class FusedComm(CollectiveComm):
             _native.cuda().fused_rs_d2h(b.ptrs, b.sigs, self.rank, self.world, s, e - s, out,
                                         1.0 / self.world, b.next_epoch(), b.counter, self.err)
 
+    def sync_grads_range(self, st: LayerRuntimeState, src: torch.Tensor, stream: Stream,
+                         lo: int, hi: int) -> None:
+        """Reduce-scatter elements [lo, hi) of the layer gradient as soon as
+        they are final (one launch per parameter tensor, in backward order),
+        so the NVLink pull and the host store overlap the rest of the
+        layer's backward.  Every rank launches for every range, also when
+        its shard misses the range (that launch only handshakes)."""
+        s, e = shard_bounds(st.numel, self.world, self.rank)
+        a, b_ = max(lo, s), min(hi, e)
+        n = max(0, b_ - a)
+        buf = self._buf(src)
+        if n and st.grad_host is not None:
+            out = st.grad_host[a - s: a - s + n]
+        else:
+            out, a, n = torch.empty(0, dtype=src.dtype), lo, 0
+        with stream.ctx():
+            _native.cuda().fused_rs_d2h(buf.ptrs, buf.sigs, self.rank, self.world, a, n, out,
+                                        1.0 / self.world, buf.next_epoch(), buf.counter, self.err)
+
+    @property
+    def grads_by_range(self) -> bool:
+        return self.fused_grads
+
     # shard-mode forward: layer fetch fused with the QKV projection -----
     def can_fuse_qkv(self, st: LayerRuntimeState) -> bool:
         return self.fused_params and st.kind == "decoder" and self.device.type == "cuda"

@@ -499,6 +499,28 @@ class SlideFSDP(nn.Module):
         st.unit = None
         st.bind_host()
 
+    def _grad_ready_hook(self, st: LayerRuntimeState):
+        """Per-tensor gradient sync during a decoder layer's backward (fused
+        NVLink reduce-scatter only): each weight gradient starts its
+        reduce-scatter + host store on the gradient stream as soon as it is
+        final, overlapping the rest of the layer's backward."""
+        if not getattr(self.comm, "grads_by_range", False) or st.unit is None:
+            return None
+        base = st.unit.grad.data_ptr()
+        es = st.unit.grad.element_size()
+        st.synced = []
+
+        def ready(t: torch.Tensor) -> None:
+            lo = (t.data_ptr() - base) // es
+            hi = lo + t.numel()
+            self.grad_stream.wait(Event(self.device).record())
+            tok = self.tracer.begin("grad_sync", st.idx, self.grad_stream)
+            self.comm.sync_grads_range(st, st.unit.grad, self.grad_stream, lo, hi)
+            self.tracer.end(tok)
+            st.synced.append((lo, hi))
+
+        return ready
+
     def _offload_grads(self, st: LayerRuntimeState, step: int) -> None:
         """After the backward of ``st``: move gradients to the host, free
         the unit, schedule the optimizer update."""
@@ -506,7 +528,19 @@ class SlideFSDP(nn.Module):
         self.grad_stream.wait(computed)
         unit = st.unit
         tok = self.tracer.begin("grad_sync", st.idx, self.grad_stream)
-        self.comm.sync_grads(st, unit.grad, self.grad_stream)
+        synced = getattr(st, "synced", None)
+        if synced:
+            # the ranges not synced during the backward (the norm weights)
+            pos = 0
+            for lo, hi in sorted(synced):
+                if lo > pos:
+                    self.comm.sync_grads_range(st, unit.grad, self.grad_stream, pos, lo)
+                pos = max(pos, hi)
+            if pos < st.numel:
+                self.comm.sync_grads_range(st, unit.grad, self.grad_stream, pos, st.numel)
+            st.synced = []
+        else:
+            self.comm.sync_grads(st, unit.grad, self.grad_stream)
         self.tracer.end(tok)
         ready = self.grad_stream.record()
         self._release(st, ready)
@@ -642,7 +676,7 @@ class SlideFSDP(nn.Module):
                 del h_in
             else:
                 saved = saved_all.pop(i)
-            dh = st.module.backward(saved, dh, ctx)
+            dh = st.module.backward(saved, dh, ctx, grad_ready=self._grad_ready_hook(st))
             del saved
             self.tracer.end(tok)
             self._offload_grads(st, step)
