@@ -6,7 +6,8 @@
 //     or the bf16 shadow) and store it into every peer's pool unit over
 //     NVLink (P2P stores; no multicast), then publish per-256-row-block
 //     arrival flags in every peer's signal pad;
-//   * the tcgen05 GEMM warps compute qkv = x * W_qkv^T from the *local* unit:
+//   * the tcgen05 GEMM warps (CTA pairs, cta_group::2, by default; single
+//     CTAs when the GEMM mode is 0) compute qkv = x * W_qkv^T from the *local* unit:
 //     before TMA-loading the B rows of a tile, the producer waits (bounded)
 //     for the arrival flags of the ranks that own those rows, then fences
 //     the generic-proxy writes for the async proxy.
@@ -14,11 +15,13 @@
 // The kernel returns once every rank's shard has landed in this GPU's unit,
 // so later kernels in the stream see the whole layer.
 #include "gemm_core.cuh"
+#include "gemm_pair.cuh"
 
 namespace t1 {
 
 CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer);
 torch::Tensor& gemm_error_word();
+int64_t gemm_get_mode();
 
 // shards: CPU int64 [world, 2] = (start, end) of every rank's shard of the
 // layer (identical on all ranks); host_src is this rank's shard.
@@ -112,11 +115,32 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
   p.ldc = out.stride(0);
   p.R = nullptr;
   p.ldr = 0;
+  p.k_blocks = (K + gemm::BK - 1) / gemm::BK;
+  p.err = gemm_error_word().data_ptr<int>();
+  if (gemm_get_mode() == 1) {
+    // CTA pairs: 256 x 256 tiles, the B row blocks match the arrival flags
+    p.tiles_m = (M + gemm::PAIR_BM - 1) / gemm::PAIR_BM;
+    p.tiles_n = (n_rows + gemm::PAIR_BN - 1) / gemm::PAIR_BN;
+    p.num_tiles = p.tiles_m * p.tiles_n;
+    CUtensorMap ta = make_map(x.data_ptr(), K, M, x.stride(0), gemm::PAIR_HALF);
+    CUtensorMap tb = make_map(unit.data_ptr(), K, n_rows, K, gemm::PAIR_HALF);
+    auto kern = gemm::gemm_pair_kernel<false, false, gemm::kStore, true>;
+    static bool pair_configured = false;
+    if (!pair_configured) {
+      T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         gemm::PAIR_SMEM_BYTES));
+      pair_configured = true;
+    }
+    // every CTA gathers, so the grid spans all SMs even when tiles are few
+    const int clusters = num_sms() / 2;
+    kern<<<2 * clusters, 256, gemm::PAIR_SMEM_BYTES, stream()>>>(ta, tb, p, ag);
+    check_launch("fused_ag_qkv (pair)");
+    count_launch();
+    return;
+  }
   p.tiles_m = (M + gemm::BM - 1) / gemm::BM;
   p.tiles_n = (n_rows + gemm::BN - 1) / gemm::BN;
   p.num_tiles = p.tiles_m * p.tiles_n;
-  p.k_blocks = (K + gemm::BK - 1) / gemm::BK;
-  p.err = gemm_error_word().data_ptr<int>();
   CUtensorMap ta = make_map(x.data_ptr(), K, M, x.stride(0), gemm::BM);
   CUtensorMap tb = make_map(unit.data_ptr(), K, n_rows, K, gemm::BN);
   auto kern = gemm::gemm_bf16_kernel<false, false, gemm::kStore, true>;

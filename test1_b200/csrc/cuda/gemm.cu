@@ -115,7 +115,8 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Para
     configured = true;
   }
   const int clusters = std::min(p.num_tiles, num_sms() / 2);
-  kern<<<2 * clusters, 192, gemm::PAIR_SMEM_BYTES, stream()>>>(ta, tb, p);
+  gemm::AgParams none{};
+  kern<<<2 * clusters, 192, gemm::PAIR_SMEM_BYTES, stream()>>>(ta, tb, p, none);
   check_launch("gemm_bf16 (pair)");
   count_launch();
 }

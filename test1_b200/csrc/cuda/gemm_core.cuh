@@ -131,6 +131,79 @@ __device__ __forceinline__ void ag_cta_range(long b, long e, long& cb, long& ce)
   ce = b + 8 * min(nv, per * static_cast<long>(blockIdx.x + 1));
 }
 
+// Gather warps (threads 192-255) of the AG variants: copy this rank's
+// shard of the layer from host memory into every peer's unit, one 256-row
+// block of the QKV weight after another, publishing each block's arrival
+// in every peer's signal pad, then everything after the QKV rows; the last
+// CTA waits until every peer's shard has landed here.
+__device__ __forceinline__ void ag_gather_warps(const AgParams& ag, const ErrorSlot& err,
+                                                volatile int* abort_flag) {
+    // ------------------------------------------- gather warps (AG only)
+    const int gt = threadIdx.x - 192;
+    const uint32_t* pad = reinterpret_cast<const uint32_t*>(ag.sig[ag.rank]);
+    if (blockIdx.x == 0 && gt == 0) ag_signal_all(ag, ag.rank);  // my unit is free
+    __shared__ int ag_ok;
+    if (gt == 0) {
+      bool ok = true;
+      for (int q = 0; q < ag.world && ok; ++q) ok = ag_wait_geq(pad + q, ag.epoch);
+      ag_ok = ok;
+      if (!ok) {
+        err.set(122);
+        *abort_flag = 1;
+      }
+    }
+    ag_named_barrier();
+    if (ag_ok) {
+      const long s0 = ag.shard_off, s1 = ag.shard_off + ag.shard_n;
+      for (int b = 0; b <= ag.n_blocks; ++b) {
+        // block b of the weight rows, then (b == n_blocks) everything after them
+        const long lo = max(s0, static_cast<long>(b) * ag.block_elems);
+        const long hi = b < ag.n_blocks ? min(s1, static_cast<long>(b + 1) * ag.block_elems) : s1;
+        if (lo >= hi) continue;
+        long cb, ce;
+        ag_cta_range(lo, hi, cb, ce);
+        ag_copy(ag, cb, ce, gt);
+        if (b < ag.n_blocks) {
+          __threadfence_system();
+          ag_named_barrier();
+          if (gt == 0) {
+            if (atomicAdd(&ag.counters[b], 1) == static_cast<int>(gridDim.x) - 1) {
+              atomicExch(&ag.counters[b], 0);
+              ag_signal_all(ag, 2 * ag.world + b * ag.world + ag.rank);
+            }
+          }
+        }
+      }
+      // tail elements (shard_n % 8) by CTA 0
+      if (blockIdx.x == 0) {
+        for (long j = ((s1 >> 3) << 3) + gt; j < s1; j += 64) {
+          const long local = j - s0;
+          bf16 v;
+          if (ag.src_kind == 0) {
+            v = static_cast<const bf16*>(ag.host_src)[local];
+          } else if (ag.src_kind == 1) {
+            v = __float2bfloat16_rn(static_cast<const float*>(ag.host_src)[local]);
+          } else {
+            const uint32_t b = ((static_cast<uint32_t>(static_cast<const uint16_t*>(ag.host_src)[local]) << 16) |
+                                static_cast<const uint16_t*>(ag.host_src_lo)[local]) - 0x8000u;
+            v = __float2bfloat16_rn(__uint_as_float(b));
+          }
+          for (int q = 0; q < ag.world; ++q) reinterpret_cast<bf16*>(ag.peer[q])[j] = v;
+        }
+      }
+      __threadfence_system();
+      ag_named_barrier();
+      if (gt == 0 && atomicAdd(&ag.counters[kAgMaxBlocks], 1) == static_cast<int>(gridDim.x) - 1) {
+        // last CTA: everything this rank owns is out; wait for every peer's
+        ag_signal_all(ag, ag.world + ag.rank);
+        bool ok = true;
+        for (int q = 0; q < ag.world && ok; ++q) ok = ag_wait_geq(pad + ag.world + q, ag.epoch);
+        if (!ok) err.set(123);
+        atomicExch(&ag.counters[kAgMaxBlocks], 0);
+      }
+    }
+}
+
 template <bool A_MN, bool B_MN, int EPI, bool AG>
 __global__ void __launch_bounds__(AG ? 256 : 192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -287,70 +360,7 @@ __global__ void __launch_bounds__(AG ? 256 : 192, 1)
       }
     }
   } else if (AG && warp >= 6) {
-    // ------------------------------------------- gather warps (AG only)
-    const int gt = threadIdx.x - 192;
-    const uint32_t* pad = reinterpret_cast<const uint32_t*>(ag.sig[ag.rank]);
-    if (blockIdx.x == 0 && gt == 0) ag_signal_all(ag, ag.rank);  // my unit is free
-    __shared__ int ag_ok;
-    if (gt == 0) {
-      bool ok = true;
-      for (int q = 0; q < ag.world && ok; ++q) ok = ag_wait_geq(pad + q, ag.epoch);
-      ag_ok = ok;
-      if (!ok) {
-        err.set(122);
-        *abort_flag = 1;
-      }
-    }
-    ag_named_barrier();
-    if (ag_ok) {
-      const long s0 = ag.shard_off, s1 = ag.shard_off + ag.shard_n;
-      for (int b = 0; b <= ag.n_blocks; ++b) {
-        // block b of the weight rows, then (b == n_blocks) everything after them
-        const long lo = max(s0, static_cast<long>(b) * ag.block_elems);
-        const long hi = b < ag.n_blocks ? min(s1, static_cast<long>(b + 1) * ag.block_elems) : s1;
-        if (lo >= hi) continue;
-        long cb, ce;
-        ag_cta_range(lo, hi, cb, ce);
-        ag_copy(ag, cb, ce, gt);
-        if (b < ag.n_blocks) {
-          __threadfence_system();
-          ag_named_barrier();
-          if (gt == 0) {
-            if (atomicAdd(&ag.counters[b], 1) == static_cast<int>(gridDim.x) - 1) {
-              atomicExch(&ag.counters[b], 0);
-              ag_signal_all(ag, 2 * ag.world + b * ag.world + ag.rank);
-            }
-          }
-        }
-      }
-      // tail elements (shard_n % 8) by CTA 0
-      if (blockIdx.x == 0) {
-        for (long j = ((s1 >> 3) << 3) + gt; j < s1; j += 64) {
-          const long local = j - s0;
-          bf16 v;
-          if (ag.src_kind == 0) {
-            v = static_cast<const bf16*>(ag.host_src)[local];
-          } else if (ag.src_kind == 1) {
-            v = __float2bfloat16_rn(static_cast<const float*>(ag.host_src)[local]);
-          } else {
-            const uint32_t b = ((static_cast<uint32_t>(static_cast<const uint16_t*>(ag.host_src)[local]) << 16) |
-                                static_cast<const uint16_t*>(ag.host_src_lo)[local]) - 0x8000u;
-            v = __float2bfloat16_rn(__uint_as_float(b));
-          }
-          for (int q = 0; q < ag.world; ++q) reinterpret_cast<bf16*>(ag.peer[q])[j] = v;
-        }
-      }
-      __threadfence_system();
-      ag_named_barrier();
-      if (gt == 0 && atomicAdd(&ag.counters[kAgMaxBlocks], 1) == static_cast<int>(gridDim.x) - 1) {
-        // last CTA: everything this rank owns is out; wait for every peer's
-        ag_signal_all(ag, ag.world + ag.rank);
-        bool ok = true;
-        for (int q = 0; q < ag.world && ok; ++q) ok = ag_wait_geq(pad + ag.world + q, ag.epoch);
-        if (!ok) err.set(123);
-        atomicExch(&ag.counters[kAgMaxBlocks], 0);
-      }
-    }
+    ag_gather_warps(ag, err, abort_flag);
   } else {
     // --------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access

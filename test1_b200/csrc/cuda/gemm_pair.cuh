@@ -30,10 +30,14 @@ constexpr int PAIR_B_BYTES = PAIR_HALF * BK * 2;
 constexpr int PAIR_STAGE_BYTES = PAIR_A_BYTES + PAIR_B_BYTES;
 constexpr int PAIR_SMEM_BYTES = PAIR_STAGES * PAIR_STAGE_BYTES + 1024 + 256;
 
-template <bool A_MN, bool B_MN, int EPI>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+// AG = true: the shard-mode fused all-gather variant (see gemm_core.cuh and
+// fused_ag_gemm.cu): two more warps per CTA copy this rank's host shard of
+// the layer into every peer's unit, and the producers wait for the B rows
+// of a tile to arrive before loading them.
+template <bool A_MN, bool B_MN, int EPI, bool AG = false>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
-                     const __grid_constant__ CUtensorMap tma_b, const Params p) {
+                     const __grid_constant__ CUtensorMap tma_b, const Params p, const AgParams ag) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -89,6 +93,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         raster(tile, p.tiles_m, p.tiles_n, mb, nb);
         const int row_a = mb * PAIR_BM + static_cast<int>(crank) * PAIR_HALF;
         const int row_b = nb * PAIR_BN + static_cast<int>(crank) * PAIR_HALF;
+        if (AG && nb < ag.n_blocks) {
+          // the B rows of this tile must have arrived from their owner ranks
+          const uint32_t* pad = reinterpret_cast<const uint32_t*>(ag.sig[ag.rank]);
+          bool ok = true;
+          for (int q = 0; q < ag.world && ok; ++q)
+            if (ag.owners[nb] & (1u << q))
+              ok = ag_wait_geq(pad + 2 * ag.world + nb * ag.world + q, ag.epoch);
+          if (!ok) {
+            err.set(115);
+            *abort_flag = 1;
+            break;
+          }
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             err.set(111);
@@ -165,6 +183,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         mma_commit_pair(&tfull[acc], 0x3);
       }
     }
+  } else if (AG && warp >= 6) {
+    ag_gather_warps(ag, err, abort_flag);
   } else {
     // --------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
