@@ -47,9 +47,26 @@ def parse_args():
     p.add_argument("--grad-sync-mode", default="gpu_reduce", choices=["gpu_reduce", "cpu_reduce"])
     p.add_argument("--pool", type=int, default=2)
     p.add_argument("--ac-offload", default="cpu", choices=["cpu", "nvme", "none"])
+    p.add_argument("--master-layout", default="split", choices=["split", "fp32", "bf16"])
+    p.add_argument("--state-dtype", default="fp32", choices=["fp32", "bf16"])
+    p.add_argument("--baseline-config", type=int, default=2, choices=[2, 3, 4],
+                   help="BASELINE.json config preset: 2 = 8B full + gpu_reduce, batch 4 x 1024 (default); "
+                        "3 = 8B shard + gpu_reduce, AC cpu, batch 2 x 4096; 4 = 70B shard + cpu_reduce, "
+                        "bf16 weights and Adam state in host RAM, batch 1 x 2048")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--profile-json", default="")
-    return p.parse_args()
+    args = p.parse_args()
+    given = {a.split("=")[0] for a in sys.argv[1:] if a.startswith("--")}
+    presets = {
+        3: dict(model="llama31_8b", param_transfer_mode="shard", grad_sync_mode="gpu_reduce",
+                batch=2, seq=4096, ac_offload="cpu"),
+        4: dict(model="llama_70b", param_transfer_mode="shard", grad_sync_mode="cpu_reduce",
+                batch=1, seq=2048, ac_offload="cpu", master_layout="bf16", state_dtype="bf16"),
+    }
+    for k, v in presets.get(args.baseline_config, {}).items():
+        if "--" + k.replace("_", "-") not in given:  # explicit flags win
+            setattr(args, k, v)
+    return args
 
 
 class ClockSampler:
@@ -154,7 +171,8 @@ def run_ours(args, rank, world, local):
                           param_transfer_mode=args.param_transfer_mode,
                           grad_sync_mode=args.grad_sync_mode, gpu_buffer_pool_size=args.pool,
                           lr=1e-5, weight_decay=0.01, ac_offload_mode=args.ac_offload,
-                          max_seq_length=args.seq, train_batch_size=args.batch, seed=42)
+                          max_seq_length=args.seq, train_batch_size=args.batch, seed=42,
+                          master_layout=args.master_layout, optimizer_state_dtype=args.state_dtype)
     t0 = time.time()
     engine = SlideFSDP(model, cfg)
     init_s = time.time() - t0
@@ -285,7 +303,10 @@ def main():
         "dtype": "bf16",
         "data": "synthetic uniform-random tokens, random-init N(0,0.02) weights",
         "config": {
-            "model": "Llama-3.1-8B architecture" if args.model == "llama31_8b" else args.model,
+            "model": {"llama31_8b": "Llama-3.1-8B architecture",
+                      "llama_70b": "Llama-70B architecture"}.get(args.model, args.model),
+            "baseline_config": args.baseline_config,
+            "master_layout": args.master_layout, "optimizer_state_dtype": args.state_dtype,
             "global_batch": args.batch * world, "seq_len": args.seq,
             "parallelism": f"dp{world}",
             "param_transfer_mode": args.param_transfer_mode, "grad_sync_mode": args.grad_sync_mode,
