@@ -474,9 +474,12 @@ static void check_qkv(const torch::Tensor& qkv, int64_t n_q, int64_t n_kv, int64
 
 std::vector<torch::Tensor> attention_fwd_tc(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                             int64_t S);
+void attention_bwd_tc_core(torch::Tensor dout, torch::Tensor qkv, torch::Tensor lse,
+                           torch::Tensor delta, torch::Tensor dq_acc, torch::Tensor dqkv, int64_t n_q,
+                           int64_t n_kv, int64_t S);
 
-// Forward implementation: 0 = mma.sync tiles (this file), 1 = tcgen05
-// (attention_tc.cu).  Per process: attn_set_mode() or T1_ATTN_TC=1.
+// Implementation of forward and backward: 0 = mma.sync tiles (this file),
+// 1 = tcgen05 (attention_tc.cu).  Per process: attn_set_mode() or T1_ATTN_TC=1.
 static int& attn_mode() {
   static int mode = [] {
     const char* e = std::getenv("T1_ATTN_TC");
@@ -533,18 +536,22 @@ torch::Tensor attention_bwd(torch::Tensor dout, torch::Tensor qkv, torch::Tensor
         delta.data_ptr<float>(), T, n_q);
     check_launch("attention_bwd_delta");
   }
-  const int smem = 6 * attn::TILE_BYTES + 64 * 128 + 4 * 64 * 4;
-  static bool cfg = false;
-  if (!cfg) {
-    T1_CHECK_CUDA(cudaFuncSetAttribute(attn::attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    cfg = true;
+  if (attn_mode() == 1) {
+    attention_bwd_tc_core(dout, qkv, lse, delta, dq_acc, dqkv, n_q, n_kv, S);
+  } else {
+    const int smem = 6 * attn::TILE_BYTES + 64 * 128 + 4 * 64 * 4;
+    static bool cfg = false;
+    if (!cfg) {
+      T1_CHECK_CUDA(cudaFuncSetAttribute(attn::attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      cfg = true;
+    }
+    dim3 grid(S / attn::BC, n_kv, B);
+    attn::attn_bwd_kernel<<<grid, 128, smem, stream()>>>(
+        (const __nv_bfloat16*)qkv.data_ptr(), qkv.stride(0), (const __nv_bfloat16*)dout.data_ptr(),
+        dout.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
+        (__nv_bfloat16*)dqkv.data_ptr(), dqkv.stride(0), S, T, n_q, n_kv, 1.0f / std::sqrt((float)D));
+    check_launch("attention_bwd");
   }
-  dim3 grid(S / attn::BC, n_kv, B);
-  attn::attn_bwd_kernel<<<grid, 128, smem, stream()>>>(
-      (const __nv_bfloat16*)qkv.data_ptr(), qkv.stride(0), (const __nv_bfloat16*)dout.data_ptr(),
-      dout.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(), dq_acc.data_ptr<float>(),
-      (__nv_bfloat16*)dqkv.data_ptr(), dqkv.stride(0), S, T, n_q, n_kv, 1.0f / std::sqrt((float)D));
-  check_launch("attention_bwd");
   const long n8 = T * n_q * D / 8;
   attn::attn_dq_convert_kernel<<<(n8 + 255) / 256, 256, 0, stream()>>>(
       dq_acc.data_ptr<float>(), (__nv_bfloat16*)dqkv.data_ptr(), dqkv.stride(0), T, n_q);

@@ -52,6 +52,14 @@ struct Params {
   int* err;
 };
 
+// 2^x with the hardware's approximate base-2 exponential (MUFU.EX2; ~2 ulp,
+// flushes denormals): the softmax weights feed a bf16 operand anyway.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // K-major 128-row operand made of two 64-column swizzled boxes: descriptor
 // of k-step k (16 columns) of the 128-column extent.
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int k) {
@@ -198,7 +206,7 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      // scores of this row: 4 chunks of 32 columns
+      // raw scores of this row: 4 chunks of 32 columns
       float sv[BN];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -206,30 +214,44 @@ __global__ void __launch_bounds__(192, 1)
         tmem_ld_32x32b_x32(t_s0 + st * BN + lane_base + c * 32, u);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[i]) * p.scale_log2;
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[i]);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[st]);
-      // causal mask (diagonal block) and keys past the sequence end
+      // causal mask: only the diagonal block and a block crossing the
+      // sequence end need it (every other key precedes every query here)
       const int kbase = j * BN;
-      float mx = m;
+      if (kbase + BN - 1 > q0 || kbase + BN > p.S) {
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        const int kpos = kbase + i;
-        if (kpos > qpos || kpos >= p.S) sv[i] = -INFINITY;
-        mx = fmaxf(mx, sv[i]);
+        for (int i = 0; i < BN; ++i) {
+          const int kpos = kbase + i;
+          if (kpos > qpos || kpos >= p.S) sv[i] = -INFINITY;
+        }
       }
-      const float alpha = (mx == -INFINITY) ? 1.f : exp2f(m - mx);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) mx = fmaxf(mx, sv[i]);
+      mx *= p.scale_log2;
+      // Lazy rescaling: the exponent base m moves only when this block's
+      // maximum exceeds it by more than 8 (a factor 256), so most blocks
+      // skip the O rescale; p = 2^(s - m) then stays below 256, far inside
+      // fp32 and bf16 range, and O / l and the LSE use the same m.
+      float alpha = 1.f;
+      if (__any_sync(0xffffffffu, mx > m + 8.f)) {
+        const float m_new = fmaxf(m, mx);
+        alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
+        m = m_new;
+      }
       float sum = 0.f;
+      const float mb = (m == -INFINITY) ? 0.f : m;
 #pragma unroll
       for (int i = 0; i < BN; ++i) {
-        const float e = (mx == -INFINITY) ? 0.f : exp2f(sv[i] - mx);
+        const float e = ex2_approx(fmaf(sv[i], p.scale_log2, -mb));
         sv[i] = e;
         sum += e;
       }
       l = l * alpha + sum;
-      m = mx;
       // P_j may overwrite the P buffer once P_{j-1} V_{j-1} completed; that
       // completion also makes O hold every block before j
       if (j > 0) {
@@ -254,7 +276,7 @@ __global__ void __launch_bounds__(192, 1)
         *reinterpret_cast<uint4*>(sP + box * BOX + r * 128 + ((u ^ (r & 7)) << 4)) = pk;
       }
       fence_proxy_async_smem();
-      // rescale O when this warp's maximum moved (alpha == 1 otherwise)
+      // rescale O when this warp moved its exponent base (alpha == 1 otherwise)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -315,7 +337,333 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+
+// ------------------------------------------------------------------ backward
+// One CTA per (128-key block, KV head, sequence); it loops over the query
+// heads of its group and the query blocks at or after its key block.  TMEM
+// (512 columns): S | dP | dK | dV, 128 columns each; dQ of a query block
+// reuses the S columns once P and dS are in shared memory.
+//   MMA1:  S = Q K^T, dP = dO V^T
+//   warps 2-5 (thread r = query row): P = exp2(S*scale*log2e - lse*log2e)
+//          (causal mask), dS = P (dP - delta); P and dS -> shared memory
+//   MMA2:  dV += P^T dO, dK += dS^T Q, dQ = dS K
+//   warps 2-5: dQ * scale -> fp32 global accumulation (vector atomics);
+//          after the last block, dK * scale and dV -> bf16 dqkv.
+// Q/dO are single-buffered: the next pair is loaded while the softmax warps
+// drain dQ.
+constexpr int BWD_SMEM_BYTES = 6 * TILE + 1024 + 256;
+
+struct BwdParams {
+  int S, T, n_q, n_kv;
+  float scale, scale_log2;
+  const float* lse;    // [Hq, T], natural log
+  const float* delta;  // [Hq, T]
+  float* dq_acc;       // [T, Hq, D]
+  bf16* dqkv;
+  long ldd;
+  int* err;
+};
+
+// MN-major operand tile: 128 rows of the K extent, 128 MN columns in two
+// 64-column boxes; descriptor of k-step k (16 rows).
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int k) {
+  return smem_desc_sw128(base + k * 2048, BOX, 1024);
+}
+
+__global__ void __launch_bounds__(192, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tma_qkv,
+                       const __grid_constant__ CUtensorMap tma_do, const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + TILE;
+  uint8_t* sQ = sV + TILE;
+  uint8_t* sDO = sQ + TILE;
+  uint8_t* sP = sDO + TILE;
+  uint8_t* sDS = sP + TILE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + TILE);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* s_full = bars + 2;
+  uint64_t* pds_full = bars + 3;
+  uint64_t* mma2_done = bars + 4;
+  uint64_t* s_free = bars + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const ErrorSlot err{p.err};
+  const int kb = blockIdx.x;  // heavy (early) key blocks first
+  const int g = blockIdx.y;
+  const int b = blockIdx.z;
+  const int G = p.n_q / p.n_kv;
+  const int tok0 = b * p.S;
+  const int nqb = (p.S + BM - 1) / BM;
+  const int per_head = nqb - kb;
+  const int n_it = G * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qdo_full, 1);
+    mbar_init(s_full, 1);
+    mbar_init(pds_full, 4);
+    mbar_init(mma2_done, 1);
+    mbar_init(s_free, 4);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tma_qkv);
+    prefetch_tensormap(&tma_do);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_dp = tmem + 128, t_dk = tmem + 256, t_dv = tmem + 384;
+
+  if (warp == 0) {
+    // ------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      const int kcol = (p.n_q + g) * D, vcol = (p.n_q + p.n_kv + g) * D;
+      const int krow = tok0 + kb * BN;
+      mbar_arrive_expect_tx(kv_full, 2 * TILE);
+      tma_load_2d(sK, &tma_qkv, kv_full, kcol, krow);
+      tma_load_2d(sK + BOX, &tma_qkv, kv_full, kcol + 64, krow);
+      tma_load_2d(sV, &tma_qkv, kv_full, vcol, krow);
+      tma_load_2d(sV + BOX, &tma_qkv, kv_full, vcol + 64, krow);
+      for (int it = 0; it < n_it && !*abort_flag; ++it) {
+        const int h = g * G + it / per_head;
+        const int qb = kb + it % per_head;
+        if (it > 0 && !mbar_wait(mma2_done, (it - 1) & 1)) {
+          err.set(221);
+          *abort_flag = 1;
+          break;
+        }
+        const int qrow = tok0 + qb * BM;
+        mbar_arrive_expect_tx(qdo_full, 2 * TILE);
+        tma_load_2d(sQ, &tma_qkv, qdo_full, h * D, qrow);
+        tma_load_2d(sQ + BOX, &tma_qkv, qdo_full, h * D + 64, qrow);
+        tma_load_2d(sDO, &tma_do, qdo_full, h * D, qrow);
+        tma_load_2d(sDO + BOX, &tma_do, qdo_full, h * D + 64, qrow);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_KK = idesc_bf16_f32(BM, BN, false, false);  // S, dP
+      constexpr uint32_t ID_MM = idesc_bf16_f32(BN, D, true, true);     // dV, dK
+      constexpr uint32_t ID_KM = idesc_bf16_f32(BM, D, false, true);    // dQ
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV), q_addr = smem_u32(sQ);
+      const uint32_t do_addr = smem_u32(sDO), p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
+      bool ok = mbar_wait(kv_full, 0);
+      if (!ok) err.set(222);
+      for (int it = 0; ok && it < n_it && !*abort_flag; ++it) {
+        if (!mbar_wait(qdo_full, it & 1)) { err.set(223); ok = false; break; }
+        if (it > 0 && !mbar_wait(s_free, (it - 1) & 1)) { err.set(224); ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          mma_bf16(t_s, kmajor_desc(q_addr, k), kmajor_desc(k_addr, k), ID_KK, k != 0);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          mma_bf16(t_dp, kmajor_desc(do_addr, k), kmajor_desc(v_addr, k), ID_KK, k != 0);
+        mma_commit(s_full);
+        if (!mbar_wait(pds_full, it & 1)) { err.set(225); ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < BM / 16; ++k)
+          mma_bf16(t_dv, mnmajor_desc(p_addr, k), mnmajor_desc(do_addr, k), ID_MM, (it | k) != 0);
+#pragma unroll
+        for (int k = 0; k < BM / 16; ++k)
+          mma_bf16(t_dk, mnmajor_desc(ds_addr, k), mnmajor_desc(q_addr, k), ID_MM, (it | k) != 0);
+#pragma unroll
+        for (int k = 0; k < BN / 16; ++k)
+          mma_bf16(t_s, kmajor_desc(ds_addr, k), mnmajor_desc(k_addr, k), ID_KM, k != 0);
+        mma_commit(mma2_done);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // --------------------------------------------- softmax / dQ / dK dV warps
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    bool ok = true;
+    // warp-uniform bounded wait
+    auto wait_w = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+      int w = 0;
+      if (lane == 0) {
+        w = !*abort_flag && mbar_wait(bar, parity);
+        if (!w && !*abort_flag) {
+          err.set(code);
+          *abort_flag = 1;
+        }
+      }
+      return __shfl_sync(0xffffffffu, w, 0) != 0;
+    };
+    // dQ of iteration `it` (in the S columns) -> global accumulation
+    auto drain_dq = [&](int it) {
+      const int h = g * G + it / per_head;
+      const int qpos = (kb + it % per_head) * BM + r;
+      float* dst = p.dq_acc + (static_cast<long>(tok0 + qpos) * p.n_q + h) * D;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(t_s + lane_base + c * 32, u);
+        tmem_ld_wait();
+        if (qpos < p.S) {
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + 4 * v),
+                      make_float4(__uint_as_float(u[4 * v]) * p.scale, __uint_as_float(u[4 * v + 1]) * p.scale,
+                                  __uint_as_float(u[4 * v + 2]) * p.scale, __uint_as_float(u[4 * v + 3]) * p.scale));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+    };
+    for (int it = 0; it < n_it; ++it) {
+      const int h = g * G + it / per_head;
+      const int qb = kb + it % per_head;
+      const int qpos = qb * BM + r;
+      const bool q_ok = qpos < p.S;
+      const float lse2 = q_ok ? p.lse[static_cast<long>(h) * p.T + tok0 + qpos] * LOG2E : 0.f;
+      const float dlt = q_ok ? p.delta[static_cast<long>(h) * p.T + tok0 + qpos] : 0.f;
+      if (it > 0) {
+        // MMA2 of it-1 done: dQ(it-1) ready, P/dS buffers free
+        if (!wait_w(mma2_done, (it - 1) & 1, 226)) { ok = false; break; }
+        tc_fence_after();
+        drain_dq(it - 1);
+      }
+      if (!wait_w(s_full, it & 1, 227)) { ok = false; break; }
+      tc_fence_after();
+      const int kbase = kb * BN;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t us[32], ud[32];
+        tmem_ld_32x32b_x32(t_s + lane_base + c * 32, us);
+        tmem_ld_32x32b_x32(t_dp + lane_base + c * 32, ud);
+        tmem_ld_wait();
+        float pv[32], dsv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int kpos = kbase + c * 32 + i;
+          const float pe = (q_ok && kpos <= qpos) ? ex2_approx(fmaf(__uint_as_float(us[i]), p.scale_log2, -lse2))
+                                                  : 0.f;
+          pv[i] = pe;
+          dsv[i] = pe * (__uint_as_float(ud[i]) - dlt);
+        }
+        // 32 keys = 4 units of 8 in box c >> 1, units (c & 1) * 4 .. + 3
+#pragma unroll
+        for (int u8 = 0; u8 < 4; ++u8) {
+          uint4 pk, dk;
+          __nv_bfloat162* hp = reinterpret_cast<__nv_bfloat162*>(&pk);
+          __nv_bfloat162* hd = reinterpret_cast<__nv_bfloat162*>(&dk);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            hp[t] = __floats2bfloat162_rn(pv[u8 * 8 + 2 * t], pv[u8 * 8 + 2 * t + 1]);
+            hd[t] = __floats2bfloat162_rn(dsv[u8 * 8 + 2 * t], dsv[u8 * 8 + 2 * t + 1]);
+          }
+          const int unit = (c & 1) * 4 + u8;
+          const uint32_t off = (c >> 1) * BOX + r * 128 + ((unit ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(sP + off) = pk;
+          *reinterpret_cast<uint4*>(sDS + off) = dk;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pds_full);
+    }
+    if (ok && n_it > 0) {
+      if (wait_w(mma2_done, (n_it - 1) & 1, 228)) {
+        tc_fence_after();
+        drain_dq(n_it - 1);
+        // dK (scaled) and dV rows: TMEM lane r = key row r of the block.  All
+        // lanes load (the TMEM loads are warp-collective); only valid rows store.
+        const int kpos = kb * BN + r;
+        const bool k_ok = kpos < p.S;
+        bf16* dk_row = p.dqkv + static_cast<long>(tok0 + kpos) * p.ldd + (p.n_q + g) * D;
+        bf16* dv_row = p.dqkv + static_cast<long>(tok0 + kpos) * p.ldd + (p.n_q + p.n_kv + g) * D;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t uk[32], uv[32];
+          tmem_ld_32x32b_x32(t_dk + lane_base + c * 32, uk);
+          tmem_ld_32x32b_x32(t_dv + lane_base + c * 32, uv);
+          tmem_ld_wait();
+          if (k_ok) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 a, bq;
+              __nv_bfloat162* ha = reinterpret_cast<__nv_bfloat162*>(&a);
+              __nv_bfloat162* hb = reinterpret_cast<__nv_bfloat162*>(&bq);
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                ha[t] = __floats2bfloat162_rn(__uint_as_float(uk[v * 8 + 2 * t]) * p.scale,
+                                              __uint_as_float(uk[v * 8 + 2 * t + 1]) * p.scale);
+                hb[t] = __floats2bfloat162_rn(__uint_as_float(uv[v * 8 + 2 * t]),
+                                              __uint_as_float(uv[v * 8 + 2 * t + 1]));
+              }
+              *reinterpret_cast<uint4*>(dk_row + c * 32 + v * 8) = a;
+              *reinterpret_cast<uint4*>(dv_row + c * 32 + v * 8) = bq;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace attn_tc
+
+
+// Backward core (tcgen05): writes dK/dV into dqkv and accumulates scaled dQ
+// into dq_acc [T, Hq, D] fp32 (zeroed by the caller); delta = rowsum(dO * O).
+void attention_bwd_tc_core(torch::Tensor dout, torch::Tensor qkv, torch::Tensor lse,
+                           torch::Tensor delta, torch::Tensor dq_acc, torch::Tensor dqkv, int64_t n_q,
+                           int64_t n_kv, int64_t S) {
+  const int64_t T = qkv.size(0), B = T / S;
+  const CUtensorMap mq = make_map(qkv.data_ptr(), qkv.size(1), T, qkv.stride(0), 128);
+  const CUtensorMap md = make_map(dout.data_ptr(), dout.size(1), T, dout.stride(0), 128);
+  attn_tc::BwdParams p;
+  p.S = static_cast<int>(S);
+  p.T = static_cast<int>(T);
+  p.n_q = static_cast<int>(n_q);
+  p.n_kv = static_cast<int>(n_kv);
+  p.scale = 1.0f / std::sqrt(static_cast<float>(attn_tc::D));
+  p.scale_log2 = p.scale * attn_tc::LOG2E;
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
+  p.ldd = dqkv.stride(0);
+  p.err = gemm_error_word().data_ptr<int>();
+  static bool cfg = false;
+  if (!cfg) {
+    T1_CHECK_CUDA(cudaFuncSetAttribute(attn_tc::attn_bwd_tc_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, attn_tc::BWD_SMEM_BYTES));
+    cfg = true;
+  }
+  dim3 grid((S + attn_tc::BN - 1) / attn_tc::BN, n_kv, B);
+  attn_tc::attn_bwd_tc_kernel<<<grid, 192, attn_tc::BWD_SMEM_BYTES, stream()>>>(mq, md, p);
+  check_launch("attention_bwd_tc");
+  count_launch();
+}
 
 std::vector<torch::Tensor> attention_fwd_tc(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                             int64_t S) {

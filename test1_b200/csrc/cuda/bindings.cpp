@@ -53,6 +53,9 @@ void multi_tensor_adam(int64_t chunk_size, torch::Tensor noop_flag,
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "test1_b200 sm_100a kernels";
   m.def("launch_count", [] { return t1::launch_counter(); });
+  m.def("clear_error", [] { return static_cast<int>(cudaGetLastError()); },
+        "Return and clear the calling thread's last CUDA runtime error (e.g. after a refused "
+        "cudaHostRegister that was handled)");
   m.def("rmsnorm_fwd", &t1::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &t1::rmsnorm_bwd);
   m.def("rope_qkv", &t1::rope_qkv);

@@ -86,6 +86,16 @@ class FusedComm(CollectiveComm):
         src = getattr(config, "shard_source", "master")
         self.shard_source = src if src in ("master", "shadow") else "master"
 
+    def disable_fused(self, params: bool, grads: bool) -> None:
+        """Fall back to the NCCL path for parameter gathers and/or gradient
+        reductions (every rank must make the same call, before the pools are
+        allocated): used when host memory a fused kernel must map could not
+        be page-locked."""
+        if params:
+            self.fused_params = False
+        if grads:
+            self.fused_grads = False
+
     # pool allocation -----------------------------------------------------
     def unit_capacity(self, numel: int) -> int:
         if self.fused_grads or self.fused_params:

@@ -53,35 +53,45 @@ class HostRegion:
     # ------------------------------------------------------------ pinning
     PIN_CHUNK = 1 << 30
 
-    def pin(self, ranges: Optional[List[tuple]] = None) -> None:
-        """Page-lock the region (portable + mapped), one registration per
-        range.  ``ranges`` are (byte offset, size) pairs on page boundaries
-        that never share a page -- one per tensor a copy or kernel reads
-        (a layer's master, its shadow, a gradient slot), so every transfer
-        lies inside a single registration.  Without ranges the region is
-        registered in 1 GiB pieces.  (A single registration of tens of GB of
-        shared memory has been refused by the OS, cudaErrorOperatingSystem.)"""
+    def pin(self, ranges: Optional[List[tuple]] = None, strict: bool = True) -> List[tuple]:
+        """Page-lock the region for this process's GPU (mapped, not portable:
+        each rank drives one device, and registering for every device of the
+        node multiplies the DMA mappings by the GPU count), one registration
+        per range.  ``ranges`` are (byte offset, size) pairs on page
+        boundaries that never share a page -- one per tensor a copy or kernel
+        reads, so every transfer lies inside a single registration.  Without
+        ranges the region is registered in 1 GiB pieces.
+
+        With ``strict=False`` a range the OS refuses stays pageable (copies
+        from it are staged by the driver; kernels cannot map it) and is
+        returned; with ``strict=True`` the first refusal raises."""
         if self.pinned:
-            return
+            return []
         rt = torch.cuda.cudart()
         base = self.buf.data_ptr()
         if ranges is None:
             ranges = [(off, min(self.PIN_CHUNK, self.nbytes - off))
                       for off in range(0, self.nbytes, self.PIN_CHUNK)]
         self._pinned_chunks = []
+        self.unpinned_ranges = []
         for off, n in ranges:
             if n <= 0:
                 continue
-            # cudaHostRegisterPortable (1) | cudaHostRegisterMapped (2)
-            rc = int(rt.cudaHostRegister(base + off, n, 3))
+            # cudaHostRegisterMapped (2): pinned and mapped for the current device
+            rc = int(rt.cudaHostRegister(base + off, n, 2))
             if rc != 0:
-                for p in self._pinned_chunks:
-                    rt.cudaHostUnregister(p)
-                self._pinned_chunks = []
-                raise RuntimeError(f"cudaHostRegister of bytes [{off}, {off + n}) of a {self.nbytes}-byte "
-                                   f"host region failed with error {rc}")
+                if strict:
+                    for p in self._pinned_chunks:
+                        rt.cudaHostUnregister(p)
+                    self._pinned_chunks = []
+                    raise RuntimeError(f"cudaHostRegister of bytes [{off}, {off + n}) of a {self.nbytes}-byte "
+                                       f"host region failed with error {rc}")
+                _native.cuda().clear_error()  # the refusal is handled: keep it out of later checks
+                self.unpinned_ranges.append((off, n))
+                continue
             self._pinned_chunks.append(base + off)
         self.pinned = True
+        return list(self.unpinned_ranges)
 
     def unpin(self) -> None:
         if self.pinned:

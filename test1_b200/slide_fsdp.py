@@ -228,9 +228,11 @@ class SlideFSDP(nn.Module):
             gbytes = torch.tensor([], dtype=self.dtype).element_size()
             self._grad_offs.append((gplan.take(gbytes * max(e - s, 0)), max(e - s, 0)))
         self.grad_region = HostRegion(max(gplan.size, 4096), pin=False)
+        grad_unpinned = []
         if self.is_cuda:
             gb = torch.tensor([], dtype=self.dtype).element_size()
-            self.grad_region.pin([(off, n * gb) for off, n in self._grad_offs if n])
+            grad_unpinned = self.grad_region.pin([(off, n * gb) for off, n in self._grad_offs if n],
+                                                 strict=False)
 
         # ---- runtime states
         self.layer_states: List[LayerRuntimeState] = []
@@ -245,8 +247,10 @@ class SlideFSDP(nn.Module):
             self.layer_states.append(st)
 
         # ---- page-lock what this rank's GPU reads or writes in the shared region
+        shared_unpinned = []
         if self.is_cuda:
-            self.shared.pin(self._pin_ranges())
+            shared_unpinned = self.shared.pin(self._pin_ranges(), strict=False)
+        self._pin_fallback(shared_unpinned, grad_unpinned)
 
         # ---- optimizer (this rank's range of every layer)
         self.layer_optimizer = self._create_optimizer(config)
@@ -314,6 +318,28 @@ class SlideFSDP(nn.Module):
             else:
                 merged.append([a, b])
         return [(a, b - a) for a, b in merged]
+
+    def _pin_fallback(self, shared_unpinned: list, grad_unpinned: list) -> None:
+        """Host ranges the OS refused to page-lock stay pageable: plain
+        copies from them still work (driver-staged, slower), but the fused
+        kernels map host memory directly, so if any rank lost a range they
+        need, every rank switches that path to the NCCL baseline."""
+        if not self.is_cuda:
+            return
+        if shared_unpinned or grad_unpinned:
+            print(f"[rank {self.rank}] warning: {len(shared_unpinned)} shared and {len(grad_unpinned)} "
+                  f"gradient host ranges could not be page-locked; copies from them are staged",
+                  flush=True)
+        flags = torch.tensor([1.0 if shared_unpinned else 0.0, 1.0 if grad_unpinned else 0.0],
+                             device=self.device)
+        if self.world_size > 1:
+            dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+        lost_params, lost_grads = (bool(x) for x in flags.tolist())
+        if (lost_params or lost_grads) and hasattr(self.comm, "disable_fused"):
+            self.comm.disable_fused(params=lost_params, grads=lost_grads)
+            if self.rank == 0:
+                print(f"fused NVLink paths disabled for: {'params ' if lost_params else ''}"
+                      f"{'grads' if lost_grads else ''} (host memory not page-locked)", flush=True)
 
     def _make_session_id(self) -> str:
         sid = [uuid.uuid4().hex[:12]]

@@ -183,3 +183,25 @@ def test_attention_tcgen05_forward_matches_reference(B, S, hq, hkv):
     assert torch.allclose(lse, lsee, atol=2e-3, rtol=1e-3)
     assert _rel(o, o0) < 1e-2
     assert torch.allclose(lse, lse0, atol=2e-3, rtol=1e-3)
+
+
+@pytest.mark.parametrize("B,S,nq,nkv", [(2, 256, 4, 2), (1, 320, 8, 2), (2, 1024, 4, 1)])
+def test_attention_tcgen05_backward_matches_reference(B, S, nq, nkv):
+    D = 128
+    T = B * S
+    g = torch.Generator(device="cuda").manual_seed(S + nq + 1)
+    qkv = torch.randn(T, (nq + 2 * nkv) * D, device="cuda", generator=g).bfloat16()
+    do = torch.randn(T, nq * D, device="cuda", generator=g).bfloat16()
+    old = native.attn_get_mode()
+    try:
+        native.attn_set_mode(1)
+        o, lse = native.attention_qkv_fwd(qkv, nq, nkv, D, S)
+        dqkv = native.attention_qkv_bwd(do, qkv, o, lse, nq, nkv, D, S)
+    finally:
+        native.attn_set_mode(old)
+    torch.cuda.synchronize()
+    dqkve = ref.attention_qkv_bwd(do.float(), qkv.float(), o.float(), lse, nq, nkv, D, S)
+    nqd, nkd = nq * D, nkv * D
+    assert _rel(dqkv[:, :nqd], dqkve[:, :nqd]) < 2e-2, "dq"
+    assert _rel(dqkv[:, nqd:nqd + nkd], dqkve[:, nqd:nqd + nkd]) < 2e-2, "dk"
+    assert _rel(dqkv[:, nqd + nkd:], dqkve[:, nqd + nkd:]) < 2e-2, "dv"
