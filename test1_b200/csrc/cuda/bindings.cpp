@@ -1,4 +1,5 @@
 // Python bindings of the sm_100a kernel library (test1_b200._cuda).
+#include <cuda_runtime.h>
 #include <torch/extension.h>
 
 #include <unordered_map>

@@ -46,8 +46,9 @@ def test_multi_tensor_adam_matches_reference(dtype, mode):
     multi_tensor_adam(1000, noop, lists, 1e-3, 0.9, 0.999, 1e-8, 3, mode, 1, 0.01)
     torch.cuda.synchronize()
     # fp32 arithmetic in the kernel (also for fp64 tensors, as in the
-    # reference's functor): a few ulps against the float64 statement
-    tol = {torch.float32: 1e-5, torch.float64: 1e-5, torch.bfloat16: 1e-2, torch.float16: 2e-3}[dtype]
+    # reference's functor), including 1 - beta2 formed in fp32 (0.999f makes
+    # it 0.00099999 instead of 0.001: a 1.3e-5 relative shift of the v update)
+    tol = {torch.float32: 1e-4, torch.float64: 1e-4, torch.bfloat16: 1e-2, torch.float16: 2e-3}[dtype]
     for (rp, rm, rv), p, m, v in zip(refs, lists[1], lists[2], lists[3]):
         for got, want in ((p, rp), (m, rm), (v, rv)):
             err = (got.double() - want).abs() / (want.abs() + 1e-3)
