@@ -479,11 +479,12 @@ void attention_bwd_tc_core(torch::Tensor dout, torch::Tensor qkv, torch::Tensor 
                            int64_t n_kv, int64_t S);
 
 // Implementation of forward and backward: 0 = mma.sync tiles (this file),
-// 1 = tcgen05 (attention_tc.cu).  Per process: attn_set_mode() or T1_ATTN_TC=1.
+// 1 = tcgen05 (attention_tc.cu, the default).  Per process: attn_set_mode()
+// or T1_ATTN_TC=0/1.
 static int& attn_mode() {
   static int mode = [] {
     const char* e = std::getenv("T1_ATTN_TC");
-    return (e != nullptr && e[0] == '1') ? 1 : 0;
+    return (e != nullptr && e[0] == '0') ? 0 : 1;  // tcgen05 unless T1_ATTN_TC=0
   }();
   return mode;
 }

@@ -515,6 +515,24 @@ class SlideFSDP(nn.Module):
         st.bind_device(with_grad=False)
         self.h2d_bytes += st.numel * unit.param.element_size()
 
+    def _check_unit(self, st: LayerRuntimeState, where: str) -> None:
+        """Debug aid (env T1_CHECK_FETCH=1): compare the device copy of a
+        layer with the bf16 rounding of its host master and report elements
+        that differ by more than one bf16 ulp."""
+        if os.environ.get("T1_CHECK_FETCH", "0") != "1" or st.unit is None or not self.is_cuda:
+            return
+        torch.cuda.synchronize(self.device)
+        dev = st.unit.param[: st.numel].float().cpu()
+        ref = st.store.read_fp32().bfloat16().float()
+        tol = ref.abs() * 2.0 ** -7 + 1e-30
+        bad = (dev - ref).abs() > tol
+        n = int(bad.sum())
+        if n:
+            idx = bad.nonzero()[:4].flatten().tolist()
+            print(f"[rank {self.rank}] T1_CHECK_FETCH {where} layer {st.idx}: {n} of {st.numel} elements differ "
+                  f"(first at {idx}: dev {[dev[i].item() for i in idx]} ref {[ref[i].item() for i in idx]})",
+                  flush=True)
+
     def _wait_loaded(self, st: LayerRuntimeState) -> None:
         if st.loaded is not None and st.loaded.e is not None:
             torch.cuda.current_stream(self.device).wait_event(st.loaded.e)
@@ -637,6 +655,7 @@ class SlideFSDP(nn.Module):
         if L > 0 and not fuse_first:
             self._fetch(S[1], with_grad=False)
         self._wait_loaded(emb)
+        self._check_unit(emb, "forward")
         with self.tracer.span("fwd", 0):
             h = emb.module.forward_ids(ctx.input_ids)
         self._release(emb, Event(dev).record())
@@ -664,6 +683,7 @@ class SlideFSDP(nn.Module):
             else:
                 h, saved_all[i] = st.module.forward_train(h, ctx, save=True, qkv_fn=qkv_fn)
             self.tracer.end(tok)
+            self._check_unit(st, "forward")
             if not fuse_qkv:
                 # prefetch the next layer(s) into free units
                 for j in range(i + 1, min(i + prefetch, L) + 1):
@@ -680,6 +700,7 @@ class SlideFSDP(nn.Module):
 
         # ---------------- output layer: loss + its backward
         self._wait_loaded(out)
+        self._check_unit(out, "forward")
         with self.tracer.span("loss", L + 1):
             loss, dh = out.module.loss_and_grad(h, ctx)
         del h
@@ -695,6 +716,7 @@ class SlideFSDP(nn.Module):
                 if self.config.enable_activation_checkpoint:
                     self.acts.prefetch(i - 1)
             self._wait_loaded(st)
+            self._check_unit(st, "backward")
             tok = self.tracer.begin("bwd", i)
             if self.config.enable_activation_checkpoint:
                 h_in = self.acts.get(i)

@@ -61,13 +61,16 @@ def test_engine_fused_matches_nccl(tmp_path, mode):
     for x, y in zip(fa["losses"], fb["losses"]):
         assert abs(x - y) < 2e-2 * abs(y)
     steps, lr = 3, 1e-3
+    bad = []
     for n, t in fb["master"].items():
         d = (fa["master"][n] - t).abs()
         # the fused path sums in fp32 and rounds once, NCCL reduces in bf16:
         # gradients agree to bf16 rounding; Adam turns a near-zero gradient's
         # rounding noise into up to +-lr per step on a few elements
-        assert d.max().item() <= 2 * lr * steps + 1e-4, n
-        assert (d > 1e-3).float().mean().item() < 0.01, n
+        frac = (d > 1e-3).float().mean().item()
+        if d.max().item() > 2 * lr * steps + 1e-4 or frac >= 0.01:
+            bad.append(f"{n}: max {d.max().item():.2e} frac>1e-3 {frac:.3f}")
+    assert not bad, "\n".join(bad)
 
 
 @pytest.mark.parametrize("src_kind", ["fp32", "bf16", "split"])

@@ -144,7 +144,18 @@ def test_cross_entropy(T, V):
 
 
 @pytest.mark.parametrize("B,S,nq,nkv", [(2, 128, 4, 2), (1, 1024, 32, 8), (2, 256, 8, 8)])
-def test_attention_fwd_bwd(B, S, nq, nkv):
+@pytest.mark.parametrize("mode", [0, 1])
+def test_attention_fwd_bwd(B, S, nq, nkv, mode):
+    """Both implementations (0 = mma.sync, 1 = tcgen05) vs the fp32 statement."""
+    old = native.attn_get_mode()
+    native.attn_set_mode(mode)
+    try:
+        _attention_fwd_bwd_case(B, S, nq, nkv)
+    finally:
+        native.attn_set_mode(old)
+
+
+def _attention_fwd_bwd_case(B, S, nq, nkv):
     D = 128
     T = B * S
     g = torch.Generator(device="cuda").manual_seed(S + nq)
