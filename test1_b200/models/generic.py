@@ -65,7 +65,7 @@ class GenericDecoderLayer(nn.Module):
             out = out[0]
         return out.reshape(B * S, -1)
 
-    def forward_train(self, h: torch.Tensor, ctx, save: bool = True, qkv_fn=None):
+    def forward_train(self, h: torch.Tensor, ctx, save: bool = True, qkv_fn=None, ln1_weight=None):
         with torch.no_grad():
             out = self._call(h, ctx)
         return out, (h if save else None)

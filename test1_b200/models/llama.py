@@ -252,13 +252,17 @@ class LlamaDecoderLayer(nn.Module):
         return g_qkv, gs[3], g_gu, gs[6], gs[7], gs[8]
 
     # forward ---------------------------------------------------------------
-    def forward_train(self, h: torch.Tensor, ctx: StepContext, save: bool = True, qkv_fn=None):
+    def forward_train(self, h: torch.Tensor, ctx: StepContext, save: bool = True, qkv_fn=None,
+                      ln1_weight=None):
         """``qkv_fn(x1)``, when given, produces the QKV projection (the engine
         passes the fused all-gather + QKV GEMM of shard mode); the other
-        weights are read after it returns."""
+        weights are read after it returns.  The input norm runs before that
+        gather, so it then takes its weight from ``ln1_weight`` (fetched on
+        its own by the engine) instead of the not-yet-filled unit."""
         cfg = self.cfg
         Hq, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
-        x1, rstd1 = ops.rmsnorm_fwd(h, self.input_layernorm.weight.data, cfg.rms_norm_eps)
+        w_ln1 = ln1_weight if ln1_weight is not None else self.input_layernorm.weight.data
+        x1, rstd1 = ops.rmsnorm_fwd(h, w_ln1, cfg.rms_norm_eps)
         if qkv_fn is not None:
             qkv = qkv_fn(x1)
         else:

@@ -533,6 +533,17 @@ class SlideFSDP(nn.Module):
                   f"(first at {idx}: dev {[dev[i].item() for i in idx]} ref {[ref[i].item() for i in idx]})",
                   flush=True)
 
+    def _early_weight(self, st: LayerRuntimeState, name: str) -> torch.Tensor:
+        """One small parameter of layer ``st`` on the device ahead of the
+        layer's fused gather: read from the shared fp32 master and rounded to
+        the compute dtype (nearest even) exactly as the gather kernel rounds
+        it, so the forward and the backward recompute agree."""
+        for e in st.layout.entries:
+            if e.name == name:
+                w = st.store.read_fp32(e.offset, e.offset + e.numel).to(self.dtype)
+                return w.view(e.shape).to(self.device, non_blocking=False)
+        raise KeyError(f"layer {st.idx} has no parameter {name}")
+
     def _wait_loaded(self, st: LayerRuntimeState) -> None:
         if st.loaded is not None and st.loaded.e is not None:
             torch.cuda.current_stream(self.device).wait_event(st.loaded.e)
@@ -667,11 +678,14 @@ class SlideFSDP(nn.Module):
         for i in range(1, L + 1):
             st = S[i]
             qkv_fn = None
+            ln1 = None
             if fuse_qkv:
-                # shard mode: the layer is gathered by its own fused QKV kernel
+                # shard mode: the layer is gathered by its own fused QKV kernel;
+                # the input norm ahead of it gets its weight separately
                 if not st.resident:
                     self._acquire_unloaded(st)
                     qkv_fn = (lambda x1, st=st: self.comm.ag_qkv(st, x1, n_qkv))
+                    ln1 = self._early_weight(st, "input_layernorm.weight")
                 else:
                     self._wait_loaded(st)
             else:
@@ -679,9 +693,9 @@ class SlideFSDP(nn.Module):
             tok = self.tracer.begin("fwd", i)
             if self.config.enable_activation_checkpoint:
                 self.acts.save(i, h, keep_on_gpu=(i == L))
-                h, _ = st.module.forward_train(h, ctx, save=False, qkv_fn=qkv_fn)
+                h, _ = st.module.forward_train(h, ctx, save=False, qkv_fn=qkv_fn, ln1_weight=ln1)
             else:
-                h, saved_all[i] = st.module.forward_train(h, ctx, save=True, qkv_fn=qkv_fn)
+                h, saved_all[i] = st.module.forward_train(h, ctx, save=True, qkv_fn=qkv_fn, ln1_weight=ln1)
             self.tracer.end(tok)
             self._check_unit(st, "forward")
             if not fuse_qkv:
