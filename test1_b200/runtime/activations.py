@@ -151,8 +151,12 @@ class ActivationStore:
                 return
             slot = self._host[i]
             self.h2d.wait(self._saved_ev.get(i))
-            buf = torch.empty(slot.shape, dtype=slot.dtype, device=self.device)
             with self.h2d.ctx():
+                # allocated on the copy stream: the caching allocator then only
+                # hands out memory whose previous users on that stream are done
+                # (memory freed by the compute stream may still be in use by its
+                # queued kernels)
+                buf = torch.empty(slot.shape, dtype=slot.dtype, device=self.device)
                 buf.copy_(slot, non_blocking=True)
             self._gpu[i] = buf
             self._loaded_ev[i] = self.h2d.record()
@@ -161,7 +165,8 @@ class ActivationStore:
         if self.mode != "nvme" or i not in self._meta:
             return
         shape, dtype, nbytes = self._meta[i]
-        out = torch.empty(shape, dtype=dtype, device=self.device)
+        with self.h2d.ctx():  # owned by the copy stream (see the cpu mode above)
+            out = torch.empty(shape, dtype=dtype, device=self.device)
         wfut = self._write_futs.pop(i, None)
 
         def read(i=i, out=out, nbytes=nbytes, wfut=wfut):
@@ -198,8 +203,11 @@ class ActivationStore:
         ev = self._loaded_ev.pop(i, None)
         if ev is not None and ev.e is not None:
             torch.cuda.current_stream(self.device).wait_event(ev.e)
-            self._gpu[i].record_stream(torch.cuda.current_stream(self.device))
-        return self._gpu.pop(i)
+        t = self._gpu.pop(i)
+        if self.cuda and (ev is not None or fut is not None):
+            # allocated on the copy stream, used from here on by this stream
+            t.record_stream(torch.cuda.current_stream(self.device))
+        return t
 
     def clear(self) -> None:
         for fut in self._read_futs.values():

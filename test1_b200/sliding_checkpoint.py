@@ -146,9 +146,11 @@ class SlidingCheckpoint(saved_tensors_hooks):
                     fut.result()
                 with open(self.file_paths[layer][k], "rb") as f:
                     f.readinto(memoryview(slot.view(torch.uint8).numpy()))
-            buf = torch.empty(shape, dtype=dtype, device=self.device)
             self.stream.wait_event(done)
             with torch.cuda.stream(self.stream):
+                # allocated on the side stream, which writes it (memory freed by
+                # the compute stream may still be in use by its queued kernels)
+                buf = torch.empty(shape, dtype=dtype, device=self.device)
                 buf.copy_(slot, non_blocking=True)
             bufs.append(buf)
         ev = self.stream.record_event()

@@ -75,3 +75,34 @@ def test_two_rank_engine_matches_oracle(tmp_path, mode, grad, sharding, ckpt):
         d = (res0["master"][n].view(p.shape) - p.detach()).abs()
         assert (d > 1e-4).float().mean().item() < 1e-3, n
         assert d.max().item() < 3 * 2 * 1e-3, n
+
+
+
+@pytest.mark.parametrize("grad", ["gpu_reduce", "cpu_reduce"])
+def test_four_rank_engine_matches_oracle(tmp_path, grad):
+    """Four ranks (three shard boundaries per layer) stay on the oracle's
+    trajectory and finite."""
+    world, steps = 4, 4
+    out = str(tmp_path / "res.pt")
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=run_engine, args=(r, world, port, "full", grad, "rank", steps, out, True))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=400)
+    errs = [f for f in os.listdir(tmp_path) if ".err" in f]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    assert all(p.exitcode == 0 for p in procs)
+    res = [torch.load(out)] + [torch.load(out + f".{r}") for r in range(1, world)]
+    oracle_losses, oracle_params = _oracle(world, steps)
+    for s in range(steps):
+        for r in range(world):
+            assert abs(res[r]["losses"][s] - oracle_losses[s][r]) < 1e-4, (s, r)
+    for n, p in oracle_params.items():
+        m = res[0]["master"][n].view(p.shape)
+        assert torch.isfinite(m).all(), n
+        d = (m - p.detach()).abs()
+        assert (d > 1e-4).float().mean().item() < 1e-3, n
+        assert d.max().item() < steps * 2 * 1e-3, n
