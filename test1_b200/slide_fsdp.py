@@ -216,6 +216,7 @@ class SlideFSDP(nn.Module):
         # ---- master stores; init (rank 0 writes), then everyone pins
         self.stores = [MasterStore(self.shared, l.numel, l.master_off, self.split_master, self.dtype,
                                    l.shadow_off, layout=self.master_layout) for l in self.layouts]
+        self._place_master_shards()
         self._init_master(model)
         if self.world_size > 1:
             dist.barrier()
@@ -318,6 +319,43 @@ class SlideFSDP(nn.Module):
             else:
                 merged.append([a, b])
         return [(a, b - a) for a, b in merged]
+
+    def _numa_node(self) -> Optional[int]:
+        """NUMA node of this rank's GPU: ``NUMA_NODE`` from the launcher, else
+        sysfs through the device's PCI address."""
+        from .runtime import numa
+
+        if os.environ.get("NUMA_NODE", "").isdigit():
+            return int(os.environ["NUMA_NODE"])
+        if not self.is_cuda:
+            return None
+        p = torch.cuda.get_device_properties(self.device)
+        bus = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        return numa.gpu_numa_node(0, bus_ids=[bus])
+
+    def _place_master_shards(self) -> None:
+        """On hosts with several NUMA nodes, before rank 0 first touches the
+        shared master, every rank gives the pages of its own optimizer shard
+        (the planes its LayerAdam threads stream every step) a preferred
+        placement on its GPU's node.  The policy lives on the shared-memory
+        object, so it applies whichever process faults the pages in.  A
+        no-op on single-node hosts."""
+        from .runtime import numa
+
+        nodes = numa.numa_nodes()
+        if len(nodes) > 1:
+            node = self._numa_node()
+            if node is not None and node in nodes:
+                host = _native.host()
+                for l, store in zip(self.layouts, self.stores):
+                    s, e = self.comm.update_range(l.numel)
+                    if e <= s:
+                        continue
+                    sl = store.optim_slice(s, e)
+                    for t in (sl if isinstance(sl, tuple) else (sl,)):
+                        host.numa_bind(t, [node], "preferred")
+        if self.world_size > 1:
+            dist.barrier()  # every policy is set before the first touch
 
     def _pin_fallback(self, shared_unpinned: list, grad_unpinned: list) -> None:
         """Host ranges the OS refused to page-lock stay pageable: plain

@@ -48,3 +48,31 @@ def test_early_weight_is_the_rounded_master():
         assert w.dtype == torch.bfloat16 and torch.equal(w.cpu(), ref.view(e.shape))
     finally:
         eng.close()
+
+
+def test_master_shards_get_numa_placement_on_multi_node_hosts(monkeypatch):
+    from test1_b200 import _native
+    from test1_b200.runtime import numa
+
+    calls = []
+    host = _native.host()
+
+    class Spy:
+        def __getattr__(self, name):
+            return getattr(host, name)
+
+        def numa_bind(self, t, nodes, mode):
+            calls.append((t.data_ptr(), t.numel(), tuple(nodes), mode))
+            return 0
+
+    monkeypatch.setattr(numa, "numa_nodes", lambda root="/": {0: [0, 1], 1: [2, 3]})
+    monkeypatch.setenv("NUMA_NODE", "1")
+    monkeypatch.setattr(_native, "host", lambda: Spy())
+    eng = _engine()
+    try:
+        # one preferred placement per plane of every layer's optimizer shard
+        assert len(calls) == 2 * eng.num_layers
+        assert all(c[2] == (1,) and c[3] == "preferred" for c in calls)
+    finally:
+        monkeypatch.undo()
+        eng.close()
