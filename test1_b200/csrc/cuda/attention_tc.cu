@@ -206,15 +206,18 @@ __global__ void __launch_bounds__(192, 1)
         break;
       }
       tc_fence_after();
-      // raw scores of this row: 4 chunks of 32 columns
+      // raw scores of this row: 4 chunks of 32 columns, all loads in flight
+      // before the one wait (one warp per scheduler: latency is the cost)
       float sv[BN];
+      {
+        uint32_t u[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(t_s0 + st * BN + lane_base + c * 32, u);
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_s0 + st * BN + lane_base + c * 32, u[c]);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[i]);
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[c][i]);
       }
       tc_fence_before();
       __syncwarp();
@@ -229,9 +232,15 @@ __global__ void __launch_bounds__(192, 1)
           if (kpos > qpos || kpos >= p.S) sv[i] = -INFINITY;
         }
       }
-      float mx = -INFINITY;
+      // row maximum: 8 independent chains, then combined (a single chain of
+      // 128 dependent max operations would stall on latency)
+      float mxs[8];
 #pragma unroll
-      for (int i = 0; i < BN; ++i) mx = fmaxf(mx, sv[i]);
+      for (int k = 0; k < 8; ++k) mxs[k] = sv[k];
+#pragma unroll
+      for (int i = 8; i < BN; ++i) mxs[i & 7] = fmaxf(mxs[i & 7], sv[i]);
+      float mx = fmaxf(fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3])),
+                       fmaxf(fmaxf(mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
       mx *= p.scale_log2;
       // Lazy rescaling: the exponent base m moves only when this block's
       // maximum exceeds it by more than 8 (a factor 256), so most blocks
@@ -243,14 +252,15 @@ __global__ void __launch_bounds__(192, 1)
         alpha = (m == -INFINITY) ? 0.f : ex2_approx(m - m_new);
         m = m_new;
       }
-      float sum = 0.f;
       const float mb = (m == -INFINITY) ? 0.f : m;
+      float sums[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < BN; ++i) {
         const float e = ex2_approx(fmaf(sv[i], p.scale_log2, -mb));
         sv[i] = e;
-        sum += e;
+        sums[i & 7] += e;
       }
+      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
       l = l * alpha + sum;
       // P_j may overwrite the P buffer once P_{j-1} V_{j-1} completed; that
       // completion also makes O hold every block before j
@@ -278,14 +288,15 @@ __global__ void __launch_bounds__(192, 1)
       fence_proxy_async_smem();
       // rescale O when this warp moved its exponent base (alpha == 1 otherwise)
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        uint32_t u[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_o + lane_base + c * 32, u[c]);
+        tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t u[32];
-          tmem_ld_32x32b_x32(t_o + lane_base + c * 32, u);
-          tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-          tmem_st_32x32b_x32(t_o + lane_base + c * 32, u);
+          for (int i = 0; i < 32; ++i) u[c][i] = __float_as_uint(__uint_as_float(u[c][i]) * alpha);
+          tmem_st_32x32b_x32(t_o + lane_base + c * 32, u[c]);
         }
         tmem_st_wait();
       }
