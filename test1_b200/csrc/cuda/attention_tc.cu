@@ -77,13 +77,18 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sP = sV + STAGES * TILE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_empty = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  // K and V of a key block have their own barriers: K's stage frees as soon
+  // as S = Q K^T is computed, so the next-but-one K block loads while P V of
+  // the current block still holds the V stage
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* s_empty = bars + 11;  // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* pv_done = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -101,8 +106,10 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 4);
     }
@@ -132,19 +139,26 @@ __global__ void __launch_bounds__(192, 1)
       tma_load_2d(sQ + BOX, &tma_qkv, q_full, qcol + 64, tok0 + q0);
       for (int j = 0; j < n_blocks && !*abort_flag; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) {
+        const uint32_t par = ((j >> 1) & 1) ^ 1;
+        uint8_t* k = sK + st * TILE;
+        uint8_t* v = sV + st * TILE;
+        const int row = tok0 + j * BN;
+        if (!mbar_wait(&k_empty[st], par)) {
           err.set(201);
           *abort_flag = 1;
           break;
         }
-        uint8_t* k = sK + st * TILE;
-        uint8_t* v = sV + st * TILE;
-        const int row = tok0 + j * BN;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
-        tma_load_2d(k, &tma_qkv, &kv_full[st], kcol, row);
-        tma_load_2d(k + BOX, &tma_qkv, &kv_full[st], kcol + 64, row);
-        tma_load_2d(v, &tma_qkv, &kv_full[st], vcol, row);
-        tma_load_2d(v + BOX, &tma_qkv, &kv_full[st], vcol + 64, row);
+        mbar_arrive_expect_tx(&k_full[st], TILE);
+        tma_load_2d(k, &tma_qkv, &k_full[st], kcol, row);
+        tma_load_2d(k + BOX, &tma_qkv, &k_full[st], kcol + 64, row);
+        if (!mbar_wait(&v_empty[st], par)) {
+          err.set(209);
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], TILE);
+        tma_load_2d(v, &tma_qkv, &v_full[st], vcol, row);
+        tma_load_2d(v + BOX, &tma_qkv, &v_full[st], vcol + 64, row);
       }
     }
   } else if (warp == 1) {
@@ -159,7 +173,7 @@ __global__ void __launch_bounds__(192, 1)
       // S(j) = Q K_j^T into S buffer j%2
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1)) { err.set(203); return false; }
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) { err.set(203); return false; }
         if (!mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1)) { err.set(204); return false; }
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sK + st * TILE);
@@ -167,6 +181,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int k = 0; k < D / 16; ++k)
           mma_bf16(t_s0 + st * BN, kmajor_desc(q_addr, k), kmajor_desc(k_addr, k), IDESC_S, k != 0);
         mma_commit(&s_full[st]);
+        mma_commit(&k_empty[st]);
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -174,6 +189,7 @@ __global__ void __launch_bounds__(192, 1)
         if (j + 1 < n_blocks && !issue_s(j + 1)) { ok = false; break; }
         // O += P_j V_j once the softmax warps published P_j (and rescaled O)
         if (!mbar_wait(p_full, j & 1)) { err.set(205); ok = false; break; }
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1)) { err.set(210); ok = false; break; }
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sV + (j & 1) * TILE);
 #pragma unroll
@@ -182,7 +198,7 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t vd = smem_desc_sw128(v_addr + k * 2048, BOX, 1024);
           mma_bf16(t_o, kmajor_desc(p_addr, k), vd, IDESC_O, (j | k) != 0);
         }
-        mma_commit(&kv_empty[j & 1]);
+        mma_commit(&v_empty[j & 1]);
         mma_commit(pv_done);
       }
       if (!ok) *abort_flag = 1;
