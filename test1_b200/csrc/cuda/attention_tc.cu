@@ -8,7 +8,9 @@
 //   warp 0      TMA producer: Q once (2 x 64-column boxes), then K and V of
 //               each 128-key block into a 2-stage ring (no multicast)
 //   warp 1      TMEM owner (384 of 512 columns: S double buffer + O) and
-//               single-thread MMA issuer:
+//               single-thread MMA issuer (P is double-buffered in shared
+//               memory, so the softmax of block j+1 never waits for P_j V_j
+//               unless it must rescale O):
 //                 S[j%2] = Q K_j^T        (M 128, N 128, K 128; A, B K-major)
 //                 O     += P_j V_j        (M 128, N 128, K 128; P K-major
 //                                          from shared memory, V MN-major)
@@ -41,7 +43,7 @@ constexpr int BOX = 128 * 64 * 2;  // one 128-row x 64-column bf16 box: 16 KB
 constexpr int TILE = 2 * BOX;      // 128 x 128 bf16 (two boxes): 32 KB
 constexpr int STAGES = 2;
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr int SMEM_BYTES = TILE /*Q*/ + STAGES * 2 * TILE /*K,V*/ + TILE /*P*/ + 1024 + 256;
+constexpr int SMEM_BYTES = TILE /*Q*/ + STAGES * 2 * TILE /*K,V*/ + 2 * TILE /*P x2*/ + 1024 + 256;
 
 struct Params {
   int S, T, n_q, n_kv, ld;  // ld: qkv row stride (elements)
@@ -74,8 +76,8 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sQ = smem;
   uint8_t* sK = sQ + TILE;
   uint8_t* sV = sK + STAGES * TILE;
-  uint8_t* sP = sV + STAGES * TILE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + TILE);
+  uint8_t* sP = sV + STAGES * TILE;  // two P buffers (block j uses j & 1)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * TILE);
   uint64_t* q_full = bars + 0;
   // K and V of a key block have their own barriers: K's stage frees as soon
   // as S = Q K^T is computed, so the next-but-one K block loads while P V of
@@ -87,8 +89,10 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* s_full = bars + 9;    // [2]
   uint64_t* s_empty = bars + 11;  // [2]
   uint64_t* p_full = bars + 13;
-  uint64_t* pv_done = bars + 14;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  // p_empty[b]: P V of the last block that used P buffer b completed (so b
+  // may be rewritten, and O holds every block up to that one)
+  uint64_t* p_empty = bars + 14;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -114,7 +118,8 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&s_empty[s], 4);
     }
     mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
+    mbar_init(&p_empty[0], 1);
+    mbar_init(&p_empty[1], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -192,14 +197,15 @@ __global__ void __launch_bounds__(192, 1)
         if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1)) { err.set(210); ok = false; break; }
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sV + (j & 1) * TILE);
+        const uint32_t pj_addr = p_addr + (j & 1) * TILE;
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k) {
           // V block: 128 keys (the K extent) x 128 dims in two 64-dim boxes
           const uint64_t vd = smem_desc_sw128(v_addr + k * 2048, BOX, 1024);
-          mma_bf16(t_o, kmajor_desc(p_addr, k), vd, IDESC_O, (j | k) != 0);
+          mma_bf16(t_o, kmajor_desc(pj_addr, k), vd, IDESC_O, (j | k) != 0);
         }
         mma_commit(&v_empty[j & 1]);
-        mma_commit(pv_done);
+        mma_commit(&p_empty[j & 1]);
       }
       if (!ok) *abort_flag = 1;
     }
@@ -278,20 +284,20 @@ __global__ void __launch_bounds__(192, 1)
       }
       const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
       l = l * alpha + sum;
-      // P_j may overwrite the P buffer once P_{j-1} V_{j-1} completed; that
-      // completion also makes O hold every block before j
-      if (j > 0) {
+      // P buffer j & 1 is free once P_{j-2} V_{j-2} completed (its
+      // (j >> 1)-th use); with the other buffer P_{j-1} V_{j-1} may still run
+      if (j > 1) {
         int w2 = 0;
-        if (lane == 0) w2 = !*abort_flag && mbar_wait(pv_done, (j - 1) & 1);
+        if (lane == 0) w2 = !*abort_flag && mbar_wait(&p_empty[j & 1], ((j >> 1) - 1) & 1);
         if (!__shfl_sync(0xffffffffu, w2, 0)) {
           if (lane == 0 && !*abort_flag) { err.set(207); *abort_flag = 1; }
           ok = false;
           break;
         }
-        tc_fence_after();
       }
       // P (bf16) into the 128B-swizzled K-major layout: row r, 16 chunks of
       // 8 keys; chunk u of a 64-key box sits at unit (u ^ (r & 7))
+      uint8_t* pbuf = sP + (j & 1) * TILE;
 #pragma unroll
       for (int c16 = 0; c16 < BN / 8; ++c16) {
         uint4 pk;
@@ -299,11 +305,24 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int t = 0; t < 4; ++t) h2[t] = __floats2bfloat162_rn(sv[c16 * 8 + 2 * t], sv[c16 * 8 + 2 * t + 1]);
         const int box = c16 >> 3, u = c16 & 7;
-        *reinterpret_cast<uint4*>(sP + box * BOX + r * 128 + ((u ^ (r & 7)) << 4)) = pk;
+        *reinterpret_cast<uint4*>(pbuf + box * BOX + r * 128 + ((u ^ (r & 7)) << 4)) = pk;
       }
       fence_proxy_async_smem();
-      // rescale O when this warp moved its exponent base (alpha == 1 otherwise)
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      // rescale O when this warp moved its exponent base (alpha == 1
+      // otherwise); O must first hold every block before j: P_{j-1} V_{j-1}
+      // is the ((j - 1) >> 1)-th completion of p_empty[(j - 1) & 1]
+      const bool rescale = j > 0 && __any_sync(0xffffffffu, alpha != 1.f);
+      if (rescale) {
+        int w3 = 0;
+        if (lane == 0) w3 = !*abort_flag && mbar_wait(&p_empty[(j - 1) & 1], ((j - 1) >> 1) & 1);
+        if (!__shfl_sync(0xffffffffu, w3, 0)) {
+          if (lane == 0 && !*abort_flag) { err.set(211); *abort_flag = 1; }
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (rescale) {
         uint32_t u[4][32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(t_o + lane_base + c * 32, u[c]);
@@ -323,7 +342,7 @@ __global__ void __launch_bounds__(192, 1)
     // epilogue: wait for the last P V, normalise, store O and the LSE
     if (ok) {
       int w = 0;
-      if (lane == 0) w = !*abort_flag && mbar_wait(pv_done, (n_blocks - 1) & 1);
+      if (lane == 0) w = !*abort_flag && mbar_wait(&p_empty[(n_blocks - 1) & 1], ((n_blocks - 1) >> 1) & 1);
       if (!__shfl_sync(0xffffffffu, w, 0)) {
         if (lane == 0 && !*abort_flag) { err.set(208); *abort_flag = 1; }
         ok = false;
