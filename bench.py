@@ -4,7 +4,7 @@ tokens/s over all GPUs (device-timed, max over ranks).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|fsdp]
     torchrun --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
 
-Config: Llama-3.1-8B architecture, random-init N(0,0.02)
+Config (comparison config 2): Llama-3.1-8B architecture, random-init N(0,0.02)
 weights, fp32 master + fp32 Adam state in pinned host memory, bf16 compute,
 param_transfer_mode=full, grad_sync_mode=gpu_reduce, gpu_buffer_pool_size=2,
 per-GPU batch 4 x 1024 uniform-random tokens, causal LM loss.  Every timed
@@ -31,7 +31,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "Llama-3.1-8B-arch tokens/sec, device-timed max over ranks, at 1/2/4/8 B200"
-BASELINE_VALUE = None  # BASELINE.md publishes no number
+BASELINE_VALUE = None  # the reference publishes no number for this metric
 
 
 def parse_args():
@@ -50,7 +50,7 @@ def parse_args():
     p.add_argument("--master-layout", default="split", choices=["split", "fp32", "bf16"])
     p.add_argument("--state-dtype", default="fp32", choices=["fp32", "bf16"])
     p.add_argument("--baseline-config", type=int, default=2, choices=[2, 3, 4],
-                   help="BASELINE.json config preset: 2 = 8B full + gpu_reduce, batch 4 x 1024 (default); "
+                   help="comparison config preset: 2 = 8B full + gpu_reduce, batch 4 x 1024 (default); "
                         "3 = 8B shard + gpu_reduce, AC cpu, batch 2 x 4096; 4 = 70B shard + cpu_reduce, "
                         "bf16 weights and Adam state in host RAM, batch 1 x 2048")
     p.add_argument("--no-e2e", action="store_true")

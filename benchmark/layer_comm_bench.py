@@ -1,4 +1,4 @@
-"""Per-layer communication microbenchmark for one
+"""Per-layer communication microbenchmark (comparison config 5) for one
 Llama-3.1-8B decoder layer (218,112,000 params, bf16 on the GPU), 2..8 GPUs:
 
   (a) shard fetch: this rank's 1/N shard of the fp32 master (split layout,

@@ -52,7 +52,7 @@ class LlamaConfig:
         if self.num_attention_heads % self.num_key_value_heads:
             raise ValueError("num_attention_heads must be a multiple of num_key_value_heads")
 
-    # ---- presets ------------------------------------
+    # ---- presets (comparison configs) ------------------------------------
     @classmethod
     def llama31_8b(cls) -> "LlamaConfig":
         return cls(
