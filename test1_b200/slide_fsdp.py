@@ -578,8 +578,12 @@ class SlideFSDP(nn.Module):
         it, so the forward and the backward recompute agree."""
         for e in st.layout.entries:
             if e.name == name:
-                w = st.store.read_fp32(e.offset, e.offset + e.numel).to(self.dtype)
-                return w.view(e.shape).to(self.device, non_blocking=False)
+                w = st.store.read_fp32(e.offset, e.offset + e.numel).to(self.dtype).view(e.shape)
+                if not self.is_cuda:
+                    return w
+                # through page-locked staging (torch's caching host allocator
+                # keeps it alive until the copy ran), so the host never waits
+                return w.pin_memory().to(self.device, non_blocking=True)
         raise KeyError(f"layer {st.idx} has no parameter {name}")
 
     def _wait_loaded(self, st: LayerRuntimeState) -> None:
