@@ -85,3 +85,19 @@ def test_generic_meta_model_initialises():
         assert torch.isfinite(eng(input_ids=ids, labels=ids).loss)
     finally:
         eng.close()
+
+
+def test_train_cli_runs_a_non_llama_checkpoint(tmp_path):
+    import subprocess
+    import sys
+
+    cfg = transformers.Qwen2Config(vocab_size=256, hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                                   num_attention_heads=4, num_key_value_heads=2, tie_word_embeddings=False)
+    transformers.Qwen2ForCausalLM(cfg).save_pretrained(str(tmp_path / "ckpt"))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(root, "train.py"), "--model-path", str(tmp_path / "ckpt"),
+                        "--device", "cpu", "--batch-size", "2", "--seq-length", "32", "--max-steps", "2",
+                        "--num-epochs", "1", "--output-dir", str(tmp_path / "out")],
+                       capture_output=True, text=True, timeout=600, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "Model type: qwen2" in r.stdout and "Training completed" in r.stdout

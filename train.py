@@ -86,6 +86,16 @@ def build_model(args, config):
     if args.model_path or config.model_path:
         path = args.model_path or config.model_path
         hf_cfg, tensors = load_hf_checkpoint(path)
+        d = hf_cfg if isinstance(hf_cfg, dict) else hf_cfg.to_dict()
+        llama_like = (d.get("model_type") in ("llama", "mistral") and not d.get("attention_bias")
+                      and not d.get("mlp_bias") and not d.get("tie_word_embeddings"))
+        if not llama_like:
+            # any other HF causal LM: its own modules, run by the engine's
+            # generic layer path (the reference loads with AutoModelForCausalLM)
+            import torch
+            from transformers import AutoModelForCausalLM
+
+            return AutoModelForCausalLM.from_pretrained(path, dtype=torch.float32)
         cfg = LlamaConfig.from_hf(hf_cfg)
         model = LlamaForCausalLM(cfg, device="meta")
         for name, p in model.named_parameters():
