@@ -131,6 +131,14 @@ class SlideFSDP(nn.Module):
         self.is_cuda = self.device.type == "cuda"
         if self.is_cuda:
             torch.cuda.set_device(self.device)
+        elif "OMP_NUM_THREADS" not in os.environ:
+            # CPU ranks compute with torch's intra-op pool; N ranks on one
+            # host with a full-size pool each oversubscribe the cores (spinning
+            # OpenMP workers slow every op by ~40x).  torchrun sets
+            # OMP_NUM_THREADS=1; other launchers get the rank's share here.
+            local_world = int(os.environ.get("LOCAL_WORLD_SIZE", "1") or 1)
+            if local_world > 1:
+                torch.set_num_threads(max(1, len(os.sched_getaffinity(0)) // local_world))
         _native.host()  # load + size the host worker pool
         if config.host_threads > 0:
             _native.host().configure_threads(config.host_threads, _native._cpu_list_from_env())
