@@ -247,6 +247,7 @@ def run_ours(args, rank, world, local):
     engine.close()
     return {
         "dev_ms": dev_ms, "e2e": e2e, "clocks": clocks, "launches": launches, "init_s": init_s,
+        "init_phases_s": dict(engine.init_times),
         "losses": losses, "h2d_gb_per_step": h2d_per_step / 1e9, "adam_busy_s_per_step": adam_busy,
         "fetch_blocked_on_adam_s_per_step": blocked, "comm": engine.comm.name,
     }
@@ -321,7 +322,7 @@ def main():
         line["impl"] = args.impl
         if args.impl == "fsdp":
             line["config"]["parallelism"] = f"fsdp{world} full_shard, CPU-offloaded params, torch AdamW"
-    extra = {k: res[k] for k in ("init_s", "h2d_gb_per_step", "adam_busy_s_per_step",
+    extra = {k: res[k] for k in ("init_s", "init_phases_s", "h2d_gb_per_step", "adam_busy_s_per_step",
                                  "fetch_blocked_on_adam_s_per_step", "comm", "losses",
                                  "attn_implementation") if k in res}
     line["detail"] = extra

@@ -125,6 +125,14 @@ class SlideFSDP(nn.Module):
         super().__init__()
         self.config = config
         self.device = torch.device(config.device)
+        self.init_times: Dict[str, float] = {}  # seconds per set-up phase
+        t_phase = [time.perf_counter()]
+
+        def phase(name: str) -> None:
+            now = time.perf_counter()
+            self.init_times[name] = round(now - t_phase[0], 3)
+            t_phase[0] = now
+
         self.dtype = config.dtype
         self.rank = dist.get_rank() if dist.is_initialized() else 0
         self.world_size = dist.get_world_size() if dist.is_initialized() else 1
@@ -156,6 +164,7 @@ class SlideFSDP(nn.Module):
         self.base_model = model
         self.model_config = model.config
         self._split_model(model)
+        phase("split_model")
 
         # ---- communication -------------------------------------------------
         self.comm = None  # built after the shared region exists (cpu_reduce slots live there)
@@ -210,6 +219,7 @@ class SlideFSDP(nn.Module):
         if self.world_size > 1 and creator:
             dist.barrier()
         self.counters = self.shared.view(torch.uint8, self._ctr_off, 8 * n_counters)
+        phase("shared_region")
 
         # ---- comm strategy (needs the slot region for cpu_reduce)
         cpu_slots = None
@@ -220,6 +230,7 @@ class SlideFSDP(nn.Module):
                                        timeout_s=config.host_wait_timeout_s, dtype=self.dtype)
         self.cpu_slots = cpu_slots
         self.comm = make_comm(config, self.device, self.rank, self.world_size, cpu_slots)
+        phase("comm")
 
         # ---- master stores; init (rank 0 writes), then everyone pins
         self.stores = [MasterStore(self.shared, l.numel, l.master_off, self.split_master, self.dtype,
@@ -228,6 +239,7 @@ class SlideFSDP(nn.Module):
         self._init_master(model)
         if self.world_size > 1:
             dist.barrier()
+        phase("master_init")
 
         # ---- per-rank host gradients (this rank's update range of each layer)
         gplan = RegionPlanner(align=4096)
@@ -242,6 +254,7 @@ class SlideFSDP(nn.Module):
             gb = torch.tensor([], dtype=self.dtype).element_size()
             grad_unpinned = self.grad_region.pin([(off, n * gb) for off, n in self._grad_offs if n],
                                                  strict=False)
+        phase("grad_region")
 
         # ---- runtime states
         self.layer_states: List[LayerRuntimeState] = []
@@ -260,9 +273,11 @@ class SlideFSDP(nn.Module):
         if self.is_cuda:
             shared_unpinned = self.shared.pin(self._pin_ranges(), strict=False)
         self._pin_fallback(shared_unpinned, grad_unpinned)
+        phase("pin_shared")
 
         # ---- optimizer (this rank's range of every layer)
         self.layer_optimizer = self._create_optimizer(config)
+        phase("optimizer")
 
         # ---- GPU buffer pools
         alloc = self.comm.allocator(self.dtype)
@@ -274,6 +289,7 @@ class SlideFSDP(nn.Module):
                                         name="embed/output-unit")
         for st in self.layer_states:
             st.pool = self.pool if st.kind == "decoder" else self.big_pool
+        phase("gpu_pools")
 
         # ---- streams, scheduler, activations
         self.h2d_stream = Stream(self.device)
@@ -516,6 +532,7 @@ class SlideFSDP(nn.Module):
         print(f"GPU buffer pool: {self.config.gpu_buffer_pool_size} units x {self.pool.capacity:,} elements "
               f"+ 1 embed/output unit x {self.big_pool.capacity:,}")
         print(f"Host SIMD: {_native.host().simd_level()}  threads: {_native.host().num_threads()}")
+        print("Set-up (s): " + ", ".join(f"{k} {v:.1f}" for k, v in self.init_times.items()))
         print("=" * 60, flush=True)
 
     def _opt_numel(self) -> int:
