@@ -60,7 +60,12 @@ def _rank_cpu_slice() -> list[int]:
 
 def cuda():
     """The sm_100a kernel library.  Importing it loads libcuda; it is only
-    needed on a machine with a B200."""
+    needed on a machine with a B200.  With ``T1_BOUNDS_CHECK=1`` the
+    bounds-checked build (``_cuda_checked``, built with
+    ``T1_BUILD_CHECKED=1``) is loaded instead; ``bounds_errors()`` then
+    reports the first out-of-range index each kernel file met."""
+    if os.environ.get("T1_BOUNDS_CHECK", "0") == "1":
+        return _load("_cuda_checked")
     return _load("_cuda")
 
 

@@ -118,6 +118,10 @@ __global__ void __launch_bounds__(128) attn_fwd_kernel(const bf16* __restrict__ 
   const int h = blockIdx.y, b = blockIdx.z;
   const int hk = h / (Hq / Hkv);
   const long tok0 = static_cast<long>(b) * S;
+  // uniform over the CTA: the query tile and the head columns exist
+  if (T1_OOB(tok0 + (qt + 1) * BR - 1, T) || T1_OOB((long)(Hq + 2 * Hkv) * D - 1, ld) ||
+      T1_OOB((long)Hq * D - 1, ldo))
+    return;
   const bf16* q_g = qkv + (tok0 + qt * BR) * ld + h * D;
   const bf16* k_g = qkv + tok0 * ld + (Hq + hk) * D;
   const bf16* v_g = qkv + tok0 * ld + (Hq + Hkv + hk) * D;
@@ -284,6 +288,10 @@ __global__ void __launch_bounds__(128) attn_bwd_kernel(
   const int nq = S / BR;
   const int g = lane >> 2, t4 = lane & 3;
   const float sl2 = scale * LOG2E;
+  // uniform over the CTA: the key tile, the sequence and the head columns exist
+  if (T1_OOB(tok0 + S - 1, T) || T1_OOB(kt, nq) || T1_OOB((long)(Hq + 2 * Hkv) * D - 1, ld) ||
+      T1_OOB((long)(Hq + 2 * Hkv) * D - 1, ldd) || T1_OOB((long)Hq * D - 1, ldo))
+    return;
 
   load_tile(sK, qkv + (tok0 + kt * BC) * ld + (Hq + hk) * D, ld, tid, 128);
   load_tile(sV, qkv + (tok0 + kt * BC) * ld + (Hq + Hkv + hk) * D, ld, tid, 128);
@@ -460,6 +468,8 @@ __global__ void attn_dq_convert_kernel(const float* __restrict__ acc, bf16* __re
 }
 
 }  // namespace attn
+
+T1_BOUNDS_READER(attention)
 
 // ================================================================ host side
 static void check_qkv(const torch::Tensor& qkv, int64_t n_q, int64_t n_kv, int64_t D, int64_t S) {

@@ -106,6 +106,9 @@ __global__ void __launch_bounds__(192, 1)
   const int tok0 = b * p.S;
   const int q0 = qb * BM;                       // first query position of this block
   const int n_blocks = min(qb + 1, (p.S + BN - 1) / BN);  // causal: key blocks 0..qb
+  // uniform over the CTA, before any barrier or TMEM is set up: the
+  // sequence lies inside the T rows and the heads inside the output row
+  if (T1_OOB(tok0 + p.S - 1, p.T) || T1_OOB((long)p.n_q * D - 1, p.ld_out)) return;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -449,6 +452,10 @@ __global__ void __launch_bounds__(192, 1)
   const int nqb = (p.S + BM - 1) / BM;
   const int per_head = nqb - kb;
   const int n_it = G * per_head;
+  // uniform over the CTA, before any barrier or TMEM is set up
+  if (T1_OOB(tok0 + p.S - 1, p.T) || T1_OOB((long)(p.n_q + 2 * p.n_kv) * D - 1, p.ldd) ||
+      T1_OOB(kb, nqb))
+    return;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -676,6 +683,8 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 }  // namespace attn_tc
+
+T1_BOUNDS_READER(attention_tc)
 
 
 // Backward core (tcgen05): writes dK/dV into dqkv and accumulates scaled dQ

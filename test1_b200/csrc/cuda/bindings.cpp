@@ -2,7 +2,11 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <string>
+#include <tuple>
 #include <unordered_map>
+#include <utility>
+#include <vector>
 
 namespace t1 {
 int64_t& launch_counter() {
@@ -49,11 +53,59 @@ void multi_tensor_adam(int64_t chunk_size, torch::Tensor noop_flag,
                        std::vector<std::vector<torch::Tensor>> tensor_lists, double lr, double beta1,
                        double beta2, double eps, int64_t step, int64_t mode, int64_t bias_correction,
                        double weight_decay);
+// per-translation-unit bounds words (bounds.cuh); always 0 outside
+// bounds-checked builds
+unsigned long long bounds_word_attention(bool);
+unsigned long long bounds_word_attention_tc(bool);
+unsigned long long bounds_word_elementwise(bool);
+unsigned long long bounds_word_embed_ce(bool);
+unsigned long long bounds_word_fused_adam(bool);
+unsigned long long bounds_word_fused_ag_gemm(bool);
+unsigned long long bounds_word_fused_comm(bool);
+unsigned long long bounds_word_gemm(bool);
+unsigned long long bounds_word_noalloc_rmsnorm(bool);
 }  // namespace t1
+
+// [(source file, line, index)] of the first out-of-bounds access each
+// kernel file recorded since the last reset; empty when none (or when the
+// library was built without T1_BOUNDS_CHECK).
+static std::vector<std::tuple<std::string, int64_t, int64_t>> bounds_errors(bool reset) {
+  using Reader = unsigned long long (*)(bool);
+  static const std::pair<const char*, Reader> readers[] = {
+      {"attention.cu", &t1::bounds_word_attention},
+      {"attention_tc.cu", &t1::bounds_word_attention_tc},
+      {"elementwise.cu", &t1::bounds_word_elementwise},
+      {"embed_ce.cu", &t1::bounds_word_embed_ce},
+      {"fused_adam.cu", &t1::bounds_word_fused_adam},
+      {"fused_ag_gemm.cu", &t1::bounds_word_fused_ag_gemm},
+      {"fused_comm.cu", &t1::bounds_word_fused_comm},
+      {"gemm.cu", &t1::bounds_word_gemm},
+      {"noalloc_rmsnorm.cu", &t1::bounds_word_noalloc_rmsnorm},
+  };
+  std::vector<std::tuple<std::string, int64_t, int64_t>> out;
+  for (const auto& r : readers) {
+    const unsigned long long w = r.second(reset);
+    if (w == ~0ull) {
+      out.emplace_back(r.first, -1, -1);  // the word could not be read
+    } else if (w != 0) {
+      int64_t idx = static_cast<int64_t>(w & ((1ull << 40) - 1));
+      if (idx & (1ll << 39)) idx -= (1ll << 40);  // sign of a negative index
+      out.emplace_back(r.first, static_cast<int64_t>(w >> 40), idx);
+    }
+  }
+  return out;
+}
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "test1_b200 sm_100a kernels";
   m.def("launch_count", [] { return t1::launch_counter(); });
+#ifdef T1_BOUNDS_CHECK
+  m.attr("bounds_checked") = true;
+#else
+  m.attr("bounds_checked") = false;
+#endif
+  m.def("bounds_errors", &bounds_errors, pybind11::arg("reset") = true,
+        "First out-of-bounds access recorded per kernel file: [(file, line, index)]");
   m.def("clear_error", [] { return static_cast<int>(cudaGetLastError()); },
         "Return and clear the calling thread's last CUDA runtime error (e.g. after a refused "
         "cudaHostRegister that was handled)");

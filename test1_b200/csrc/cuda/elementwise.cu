@@ -20,6 +20,8 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const bf16* __restrict
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int nvec = H >> 3;
+  // uniform over the CTA: the row exists and VPT vectors per thread cover it
+  if (T1_OOB(row, T) || T1_OOB(nvec - 1, VPT * (int)blockDim.x)) return;
   const bf16* xr = x + (size_t)row * H;
   float v[VPT][8];
   float ss = 0.f;
@@ -60,6 +62,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(
     float* __restrict__ dw_part, int T, int H, int rows_per_cta) {
   __shared__ float red[32];
   const int nvec = H >> 3;
+  if (T1_OOB(nvec - 1, VPT * (int)blockDim.x)) return;  // uniform over the CTA
   float wv[VPT][8], acc[VPT][8];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
@@ -147,6 +150,7 @@ __global__ void rope_qkv_kernel(bf16* __restrict__ qkv, int T, int ld, int n_rot
   const int h = th % n_rot;
   const int t = th / n_rot;
   const int pos = t % S;
+  if (T1_OOB((long)h * D + 8 * jv + half + 7, ld) || T1_OOB(pos, S)) return;
   bf16* base = qkv + (size_t)t * ld + (size_t)h * D + 8 * jv;
   float x1[8], x2[8];
   load8(base, x1);
@@ -204,6 +208,8 @@ __global__ void swiglu_bwd_kernel(const bf16* __restrict__ da, const bf16* __res
 }
 
 // ================================================================ host side
+T1_BOUNDS_READER(elementwise)
+
 static void check_rows(const torch::Tensor& t, int64_t H, const char* what) {
   TORCH_CHECK(t.dim() == 2 && t.size(1) == H && t.stride(1) == 1 && t.stride(0) == H, what,
               " must be a contiguous [T, ", H, "] tensor");

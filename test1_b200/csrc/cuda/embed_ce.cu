@@ -12,7 +12,8 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const bf16
                                      bf16* __restrict__ h, int H, int64_t V) {
   const int t = blockIdx.x;
   int64_t id = ids[t];
-  if (id < 0 || id >= V) id = 0;  // out-of-range ids are rejected on the host
+  if (T1_OOB(id, V)) return;      // checked builds: record and skip the row
+  if (id < 0 || id >= V) id = 0;  // host-resident ids are range-checked before the copy
   const int4* src = reinterpret_cast<const int4*>(w + id * H);
   int4* dst = reinterpret_cast<int4*>(h + (size_t)t * H);
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
@@ -24,9 +25,11 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const bf16
 __global__ void embedding_bwd_kernel(const int64_t* __restrict__ sorted_ids,
                                      const int64_t* __restrict__ order,
                                      const bf16* __restrict__ dh, bf16* __restrict__ dw, int T,
-                                     int H) {
+                                     int H, int64_t V) {
   const int i = blockIdx.x;
   const int64_t id = sorted_ids[i];
+  if (T1_OOB(id, V)) return;  // checked builds: record
+  if (id < 0 || id >= V) return;  // never write outside dw
   if (i > 0 && sorted_ids[i - 1] == id) return;
   int end = i + 1;
   while (end < T && sorted_ids[end] == id) ++end;
@@ -34,6 +37,7 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ sorted_ids,
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int j = i; j < end; ++j) {
       float v[8];
+      if (T1_OOB(order[j], T)) continue;
       load8(dh + (size_t)order[j] * H + c, v);
 #pragma unroll
       for (int k = 0; k < 8; ++k) acc[k] += v[k];
@@ -87,6 +91,8 @@ __global__ void __launch_bounds__(512) ce_fwd_bwd_kernel(bf16* __restrict__ logi
   const float bs = block_sum(s, red);
   const float lse = bm + __logf(bs);
   const int64_t t = tgt[row];
+  if (t != ignore && T1_OOB(t, V)) {
+  }  // checked builds: record a target that is neither ignored nor a class
   const bool valid = t != ignore && t >= 0 && t < V;
   if (threadIdx.x == 0) {
     row_loss[row] = valid ? lse - __bfloat162float(lr[t]) : 0.f;
@@ -117,6 +123,8 @@ __global__ void ce_loss_reduce_kernel(const float* __restrict__ row_loss, int T,
 }
 
 // ================================================================ host side
+T1_BOUNDS_READER(embed_ce)
+
 torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w) {
   TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == torch::kInt64, "ids must be int64 CUDA");
   T1_CHECK_INPUT(w, torch::kBFloat16);
@@ -146,7 +154,8 @@ void embedding_bwd(torch::Tensor dh, torch::Tensor ids, torch::Tensor dw) {
   auto sorted = std::get<0>(sr);
   auto order = std::get<1>(sr);
   embedding_bwd_kernel<<<T, 128, 0, stream()>>>(sorted.data_ptr<int64_t>(), order.data_ptr<int64_t>(),
-                                                (const bf16*)dh.data_ptr(), (bf16*)dw.data_ptr(), T, H);
+                                                (const bf16*)dh.data_ptr(), (bf16*)dw.data_ptr(), T, H,
+                                                dw.size(0));
   check_launch("embedding_bwd");
   count_launch();
 }

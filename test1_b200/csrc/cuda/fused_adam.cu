@@ -100,6 +100,7 @@ __global__ void __launch_bounds__(kThreads) multi_tensor_adam_kernel(const __gri
     }
     const int t = lo;
     const int64_t base = (c - tab.chunk_start[t]) * h.chunk;
+    if (T1_OOB(base, tab.n[t])) continue;  // a chunk starts inside its tensor
     const int64_t end = min(tab.n[t], base + h.chunk);
     T* g = static_cast<T*>(tab.g[t]);
     T* p = static_cast<T*>(tab.p[t]);
@@ -176,6 +177,8 @@ void launch_batch(const std::vector<std::vector<torch::Tensor>>& lists, size_t b
 }
 
 }  // namespace
+
+T1_BOUNDS_READER(fused_adam)
 
 void multi_tensor_adam(int64_t chunk_size, torch::Tensor noop_flag,
                        std::vector<std::vector<torch::Tensor>> tensor_lists, double lr, double beta1,

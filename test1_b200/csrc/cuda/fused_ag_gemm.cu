@@ -19,6 +19,8 @@
 
 namespace t1 {
 
+T1_BOUNDS_READER(fused_ag_gemm)
+
 CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer);
 torch::Tensor& gemm_error_word();
 int64_t gemm_get_mode();

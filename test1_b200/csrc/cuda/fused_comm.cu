@@ -205,6 +205,8 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, i
 }  // namespace fused
 
 // ================================================================ host side
+T1_BOUNDS_READER(fused_comm)
+
 static fused::Peers make_peers(torch::Tensor ptrs, torch::Tensor sigs, int world) {
   TORCH_CHECK(world >= 1 && world <= fused::kMaxRanks, "world size must be 1..8");
   TORCH_CHECK(ptrs.device().is_cpu() && ptrs.scalar_type() == torch::kInt64 && ptrs.numel() == world,

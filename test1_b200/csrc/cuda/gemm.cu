@@ -40,6 +40,8 @@ namespace t1 {
 
 
 // ================================================================ host side
+T1_BOUNDS_READER(gemm)
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,

@@ -96,6 +96,7 @@ __device__ __forceinline__ void ag_copy(const AgParams& ag, long b, long e, int 
   for (long v = v0 + gt; v < v1; v += 64) {
     int4 out;
     const long local = 8 * v - ag.shard_off;
+    if (T1_OOB(local, ag.shard_n) || T1_OOB(local + 7, ag.shard_n)) continue;
     if (ag.src_kind == 0) {
       out = *reinterpret_cast<const int4*>(static_cast<const bf16*>(ag.host_src) + local);
     } else {
@@ -396,7 +397,7 @@ __global__ void __launch_bounds__(AG ? 256 : 192, 1)
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             const int col = col0 + 8 * v;
-            if (col < p.N) {
+            if (col < p.N && !T1_OOB(col + 7, p.ldc)) {
               float f[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);

@@ -222,7 +222,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             const int col = col0 + 8 * v;
-            if (col < p.N) {
+            if (col < p.N && !T1_OOB(col + 7, p.ldc)) {
               float f[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[8 * v + j]);

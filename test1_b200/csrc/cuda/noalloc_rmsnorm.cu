@@ -50,6 +50,8 @@
 
 #include <mutex>
 
+#include "bounds.cuh"
+
 namespace t1 {
 namespace noalloc {
 
@@ -162,7 +164,7 @@ __global__ void __launch_bounds__(kThreads) rows_kernel(const bf16* __restrict__
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int i = threadIdx.x + k * kThreads;
-    if (i < nvec) {
+    if (i < nvec && !T1_OOB(static_cast<long long>(blockIdx.x) * H + 8 * i + 7, kScratchFloats)) {
       float* dst = part + static_cast<size_t>(blockIdx.x) * H + 8 * i;
 #pragma unroll
       for (int j = 0; j < 8; ++j) dst[j] = acc[k][j];
@@ -197,6 +199,9 @@ static float* scratch_for_current_device() {
 }
 
 }  // namespace noalloc
+
+T1_BOUNDS_READER(noalloc_rmsnorm)
+
 }  // namespace t1
 
 extern "C" int t1_rmsnorm_bwd_noalloc(const __nv_bfloat16* dy, const __nv_bfloat16* x,

@@ -698,10 +698,26 @@ class SlideFSDP(nn.Module):
                 labels: Optional[torch.Tensor] = None, **kwargs) -> CausalLMOutputWithPast:
         if attention_mask is not None:
             self._check_mask(attention_mask)
+        self._check_ids(input_ids, labels)
         if labels is None:
             return CausalLMOutputWithPast(loss=None, logits=self._inference(input_ids))
         loss = self._train_step(input_ids, labels)
         return CausalLMOutputWithPast(loss=loss, logits=None)
+
+    def _check_ids(self, input_ids: torch.Tensor, labels: Optional[torch.Tensor]) -> None:
+        """Token ids and labels that arrive in host memory are range-checked
+        before they are copied (device-resident ones are not, as that would
+        synchronise every step; the kernels never access memory for an
+        out-of-range id, and the bounds-checked build records it)."""
+        V = self.model_config.vocab_size
+        if input_ids.device.type == "cpu" and input_ids.numel():
+            lo, hi = int(input_ids.min()), int(input_ids.max())
+            if lo < 0 or hi >= V:
+                raise ValueError(f"input_ids must lie in [0, {V}), got [{lo}, {hi}]")
+        if labels is not None and labels.device.type == "cpu" and labels.numel():
+            valid = labels[labels != -100]
+            if valid.numel() and (int(valid.min()) < 0 or int(valid.max()) >= V):
+                raise ValueError(f"labels must be -100 or lie in [0, {V})")
 
     def _check_mask(self, mask: torch.Tensor) -> None:
         """Causal attention without a mask is exact for right padding (no

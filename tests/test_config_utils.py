@@ -116,3 +116,14 @@ def test_split_planes_round_trip():
     assert (bf.float() - orig).abs().max() <= orig.abs().max() * 2 ** -8
     split_planes_to_fp32_(x)
     assert torch.equal(x, orig)
+
+
+def test_native_loader_selects_the_bounds_checked_build(monkeypatch):
+    from test1_b200 import _native
+
+    seen = []
+    monkeypatch.setattr(_native, "_load", lambda name: seen.append(name) or name)
+    monkeypatch.setenv("T1_BOUNDS_CHECK", "1")
+    assert _native.cuda() == "_cuda_checked"
+    monkeypatch.setenv("T1_BOUNDS_CHECK", "0")
+    assert _native.cuda() == "_cuda"

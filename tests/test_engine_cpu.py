@@ -145,3 +145,22 @@ def test_bf16_master_and_bf16_state_train():
     assert abs(a[0] - b[0]) < 1e-3
     for x, y in zip(a, b):
         assert abs(x - y) < 5e-2
+
+
+def test_out_of_range_token_ids_and_labels_are_rejected():
+    torch.manual_seed(0)
+    eng = SlideFSDP(LlamaForCausalLM(LlamaConfig.tiny()), SlideFSDPConfig(dtype=torch.float32, device="cpu"))
+    try:
+        ids = torch.randint(0, 1024, (1, 16))
+        bad = ids.clone()
+        bad[0, 3] = 1024
+        with pytest.raises(ValueError, match="input_ids"):
+            eng(input_ids=bad, labels=ids)
+        lab = ids.clone()
+        lab[0, 5] = -7
+        with pytest.raises(ValueError, match="labels"):
+            eng(input_ids=ids, labels=lab)
+        lab[0, 5] = -100  # the ignore index is fine
+        assert torch.isfinite(eng(input_ids=ids, labels=lab).loss)
+    finally:
+        eng.close()
