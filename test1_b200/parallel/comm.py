@@ -40,6 +40,7 @@ from __future__ import annotations
 import os
 import threading
 import time
+from datetime import timedelta
 from typing import List, Optional
 
 import torch
@@ -136,9 +137,13 @@ class CollectiveComm(CommStrategy):
         super().__init__(config, device, rank, world)
         backend = "nccl" if device.type == "cuda" else "gloo"
         # Separate communicators so parameter gathers and gradient reductions
-        # of neighbouring layers can run concurrently.
-        self.param_group = dist.new_group(backend=backend) if self.param_mode == "shard" else None
-        self.grad_group = dist.new_group(backend=backend)
+        # of neighbouring layers can run concurrently.  Their set-up and
+        # collectives wait for a peer at most host_wait_timeout_s (the default
+        # of new_group would be 30 minutes when a peer never arrives).
+        tmo = timedelta(seconds=max(1.0, float(getattr(config, "host_wait_timeout_s", 600.0))))
+        self.param_group = (dist.new_group(backend=backend, timeout=tmo)
+                            if self.param_mode == "shard" else None)
+        self.grad_group = dist.new_group(backend=backend, timeout=tmo)
         self.cpu_slots = cpu_slots
         self._shard_bufs = {}
 

@@ -25,9 +25,54 @@ from .. import _native
 
 ALIGN_BYTES = 4096
 
+# Header of a shared region: int64 words [magic, version, then the layout
+# fields in REGION_FIELDS order, then a checksum of all previous words].
+REGION_MAGIC = 0x4853303032423154  # "T1B200SH" little-endian
+REGION_VERSION = 1
+REGION_FIELDS = ("region_bytes", "world_size", "num_layers", "total_params", "layout_code")
+REGION_HEADER_BYTES = 8 * (3 + len(REGION_FIELDS))
+
 
 def _align(x: int, a: int = ALIGN_BYTES) -> int:
     return (x + a - 1) // a * a
+
+
+def _checksum(words: List[int]) -> int:
+    c = 0x9E3779B97F4A7C15
+    for w in words:
+        c = ((c ^ (w & 0xFFFFFFFFFFFFFFFF)) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+    return c - (1 << 64) if c >= 1 << 63 else c
+
+
+def write_region_header(region: "HostRegion", offset: int, fields: dict) -> None:
+    """The creating rank stamps the layout it carved the region for, so that
+    every rank that maps it later can tell that it expects the same one."""
+    words = [REGION_MAGIC, REGION_VERSION] + [int(fields[k]) for k in REGION_FIELDS]
+    words.append(_checksum(words))
+    region.view(torch.int64, offset, len(words)).copy_(torch.tensor(words, dtype=torch.int64))
+
+
+def check_region_header(region: "HostRegion", offset: int, fields: dict, rank: int = 0) -> None:
+    """Raise a descriptive error unless the header at ``offset`` was written
+    for exactly this layout: a region that another program wrote over, a
+    damaged header, or local ranks started with different models or
+    configurations (each would read the others' bytes as its own tensors)."""
+    words = region.view(torch.int64, offset, 3 + len(REGION_FIELDS)).tolist()
+    where = region.shm_path or "anonymous region"
+    if words[0] != REGION_MAGIC:
+        raise RuntimeError(f"rank {rank}: shared host region {where} carries no test1_b200 header "
+                           f"(magic {words[0]:#x}); it was overwritten or created by another program")
+    if words[-1] != _checksum(words[:-1]):
+        raise RuntimeError(f"rank {rank}: the header of shared host region {where} is corrupt (checksum)")
+    if words[1] != REGION_VERSION:
+        raise RuntimeError(f"rank {rank}: shared host region {where} has header version {words[1]}, "
+                           f"expected {REGION_VERSION}")
+    for k, got in zip(REGION_FIELDS, words[2:-1]):
+        want = int(fields[k])
+        if got != want:
+            raise RuntimeError(f"rank {rank}: shared host region {where} was laid out for {k} = {got}, "
+                               f"this rank expects {want}; every local rank must run the same model "
+                               f"and configuration")
 
 
 class HostRegion:

@@ -39,6 +39,7 @@ import math
 import os
 import time
 import uuid
+import zlib
 from dataclasses import dataclass
 from typing import Dict, List, Optional
 
@@ -54,7 +55,8 @@ from .optim.layer_adam import LayerAdam
 from .parallel.comm import CpuReduceSlots, make_comm
 from .runtime.activations import ActivationStore
 from .runtime.device import Event, Stream
-from .runtime.host_memory import HostRegion, MasterStore, RegionPlanner
+from .runtime.host_memory import (REGION_HEADER_BYTES, HostRegion, MasterStore, RegionPlanner,
+                                  check_region_header, write_region_header)
 from .utils.trace import PhaseTracer
 from .runtime.layer_state import (LayerBufferPool, LayerLayout, LayerRuntimeState, build_layout,
                                   shard_size)
@@ -184,6 +186,7 @@ class SlideFSDP(nn.Module):
 
         # ---- shared host region: counters | master fp32 | shadow bf16 | cpu slots
         plan = RegionPlanner(align=4096)
+        self._hdr_off = plan.take(REGION_HEADER_BYTES)
         n_counters = 4 * self.num_layers + 64
         self._ctr_off = plan.take(8 * n_counters)
         self.split_master = self.dtype == torch.bfloat16 and config.master_layout == "split"
@@ -216,8 +219,13 @@ class SlideFSDP(nn.Module):
             dist.barrier()
         self.shared = HostRegion(plan.size, shm_path=shm_path, create=creator or shm_path is None,
                                  pin=False)
+        header = self._region_fields(plan.size)
+        if creator:
+            write_region_header(self.shared, self._hdr_off, header)
         if self.world_size > 1 and creator:
             dist.barrier()
+        if not creator:
+            check_region_header(self.shared, self._hdr_off, header, self.rank)
         self.counters = self.shared.view(torch.uint8, self._ctr_off, 8 * n_counters)
         phase("shared_region")
 
@@ -343,6 +351,14 @@ class SlideFSDP(nn.Module):
             else:
                 merged.append([a, b])
         return [(a, b - a) for a, b in merged]
+
+    def _region_fields(self, nbytes: int) -> dict:
+        """What the shared region's layout depends on, for its header."""
+        c = self.config
+        desc = (f"{self.master_layout}|{self.dtype}|{c.param_transfer_mode}|{c.grad_sync_mode}|"
+                f"{c.optimizer_sharding}|{[l.numel for l in self.layouts]}")
+        return {"region_bytes": nbytes, "world_size": self.world_size, "num_layers": self.num_layers,
+                "total_params": self.total_params, "layout_code": zlib.crc32(desc.encode())}
 
     def _numa_node(self) -> Optional[int]:
         """NUMA node of this rank's GPU: ``NUMA_NODE`` from the launcher, else

@@ -44,3 +44,29 @@ def run(rank, world, port, out_path, grad_mode):
         result["trace"] = traceback.format_exc()
     torch.save(result, out_path + f".{rank}")
     os._exit(0)
+
+
+def run_mismatch(rank, world, port, out_path):
+    """Rank 1 builds a model with one layer fewer than rank 0's: it must
+    refuse the shared region rank 0 laid out instead of reading it."""
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_RANK=str(rank),
+                      LOCAL_WORLD_SIZE=str(world), T1_QUIET="1")
+    result = {"rank": rank, "error": None}
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+        from test1_b200 import SlideFSDPConfig
+        from test1_b200.models.llama import LlamaConfig, LlamaForCausalLM
+        from test1_b200.slide_fsdp import SlideFSDP
+
+        cfg = LlamaConfig.tiny()
+        if rank == 1:
+            cfg.num_hidden_layers -= 1
+        eng = SlideFSDP(LlamaForCausalLM(cfg), SlideFSDPConfig(dtype=torch.float32, device="cpu",
+                                                               host_wait_timeout_s=3.0))
+        eng.close()
+    except Exception as exc:
+        result["error"] = f"{type(exc).__name__}: {exc}"
+    torch.save(result, out_path + f".{rank}")
+    os._exit(0)

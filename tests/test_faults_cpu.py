@@ -8,7 +8,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from tests._fault_worker import run
+from tests._fault_worker import run, run_mismatch
 
 
 def _port():
@@ -53,3 +53,45 @@ def test_update_wait_timeout_names_layer():
     assert time.time() - t0 < 5
     sch.close()
     region.close()
+
+
+def test_rank_with_another_layout_refuses_the_shared_region(tmp_path):
+    out = str(tmp_path / "res")
+    ctx = mp.get_context("spawn")
+    port = _port()
+    ps = [ctx.Process(target=run_mismatch, args=(r, 2, port, out)) for r in range(2)]
+    t0 = time.time()
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=240)
+    assert time.time() - t0 < 240, "a rank hung"
+    r1 = torch.load(out + ".1")
+    assert r1["error"] is not None and "every local rank must run the same model" in r1["error"], r1
+    assert torch.load(out + ".0")["error"] is not None  # the creator's next collective fails, bounded
+
+
+def test_region_header_detects_overwrite_and_corruption(tmp_path):
+    from test1_b200.runtime.host_memory import (REGION_HEADER_BYTES, HostRegion, check_region_header,
+                                                write_region_header)
+
+    path = f"/dev/shm/t1b200_test_{os.getpid()}.bin"
+    fields = {"region_bytes": 8192, "world_size": 2, "num_layers": 6, "total_params": 12345,
+              "layout_code": 77}
+    owner = HostRegion(8192, shm_path=path, create=True)
+    try:
+        write_region_header(owner, 0, fields)
+        peer = HostRegion(8192, shm_path=path, create=False)
+        check_region_header(peer, 0, fields, rank=1)
+        with pytest.raises(RuntimeError, match="num_layers = 6, this rank expects 5"):
+            check_region_header(peer, 0, dict(fields, num_layers=5), rank=1)
+        words = owner.view(torch.int64, 0, REGION_HEADER_BYTES // 8)
+        words[4] += 1  # one flipped field: the checksum no longer matches
+        with pytest.raises(RuntimeError, match="corrupt"):
+            check_region_header(peer, 0, fields, rank=1)
+        words[0] = 0  # overwritten by something else
+        with pytest.raises(RuntimeError, match="no test1_b200 header"):
+            check_region_header(peer, 0, fields, rank=1)
+        peer.close()
+    finally:
+        owner.close()
