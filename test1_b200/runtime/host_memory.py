@@ -10,9 +10,11 @@ aligned views: the fp32 master, the bf16 shadow, gradient buffers, counters.
   zero-fill pass, and page-locked for DMA).
 * Single rank: an anonymous private mapping with transparent huge pages.
 
-Both are registered with ``cudaHostRegister`` (portable + mapped) when a GPU
-is present, so host<->device copies run at full DMA speed and kernels can
-read/write the memory directly (zero-copy).
+On a GPU each rank registers the ranges its own device reads or writes with
+``cudaHostRegister`` (mapped, for the current device only), so host<->device
+copies run at full DMA speed and kernels can read/write the memory directly
+(zero-copy).  The first words of a shared region are a header that the
+creating rank writes and every other rank checks (``check_region_header``).
 """
 from __future__ import annotations
 
