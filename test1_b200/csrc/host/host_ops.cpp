@@ -395,9 +395,16 @@ torch::Tensor shm_map(const std::string& path, int64_t bytes, bool create) {
     }
   } else {
     struct stat st;
-    fstat(fd, &st);
-    TORCH_CHECK(st.st_size >= bytes, "shm file ", path, " has ", st.st_size, " bytes, need ",
-                bytes);
+    if (fstat(fd, &st) != 0) {
+      int err = errno;
+      ::close(fd);
+      TORCH_CHECK(false, "fstat(", path, ") failed: ", std::strerror(err));
+    }
+    if (st.st_size < bytes) {
+      ::close(fd);
+      TORCH_CHECK(false, "shm file ", path, " has ", st.st_size, " bytes, need ", bytes,
+                  " (was it created for another model or configuration?)");
+    }
   }
   void* p = mmap(nullptr, bytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
   int err = errno;
