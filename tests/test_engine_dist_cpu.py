@@ -78,15 +78,17 @@ def test_two_rank_engine_matches_oracle(tmp_path, mode, grad, sharding, ckpt):
 
 
 
-@pytest.mark.parametrize("grad", ["gpu_reduce", "cpu_reduce"])
-def test_four_rank_engine_matches_oracle(tmp_path, grad):
-    """Four ranks (three shard boundaries per layer) stay on the oracle's
-    trajectory and finite."""
-    world, steps = 4, 4
+@pytest.mark.parametrize("world,mode,grad", [(4, "full", "gpu_reduce"), (4, "full", "cpu_reduce"),
+                                             (8, "full", "gpu_reduce"), (8, "shard", "gpu_reduce")])
+def test_many_rank_engine_matches_oracle(tmp_path, world, mode, grad):
+    """Four and eight ranks (up to seven shard boundaries per layer, the
+    rank count of one 8-GPU node) stay on the oracle's trajectory and
+    finite."""
+    steps = 4
     out = str(tmp_path / "res.pt")
     port = _free_port()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=run_engine, args=(r, world, port, "full", grad, "rank", steps, out, True))
+    procs = [ctx.Process(target=run_engine, args=(r, world, port, mode, grad, "rank", steps, out, True))
              for r in range(world)]
     for p in procs:
         p.start()
