@@ -3,8 +3,10 @@
 Same field names, defaults, accepted values and validation messages as the
 reference's configuration dataclass (config.py:17-165 in LaiHOLA/Test1), so
 JSON configs written for the reference load unchanged.  Fields that the
-reference accepts but ignores (``prefetch_layers``, ``max_workers``,
-``clip_grad_norm``) are honoured here.
+reference accepts but ignores are honoured here: ``prefetch_layers`` (units
+loaded ahead), ``max_workers`` and ``clip_grad_norm`` (applied before the
+updates when ``exact_grad_clip`` is set; otherwise ``clip_grad_norm_()``
+reports the norm after the fact, as in the reference).
 
 Extra fields (all optional, reference configs never set them):
     optimizer_sharding: "rank" (each rank updates 1/N of every layer, the
@@ -26,6 +28,12 @@ Extra fields (all optional, reference configs never set them):
         fit in host RAM.
     optimizer_state_dtype: dtype of LayerAdam's m and v in host memory
         ("fp32", or "bf16" to halve the state of very large models).
+    exact_grad_clip: with clip_grad_norm > 0, every step scales its
+        gradients so that their global L2 norm (over all layers and ranks)
+        is at most clip_grad_norm before any layer is updated, as
+        torch.nn.utils.clip_grad_norm_ before optimizer.step() does.  The
+        updates then start after the whole backward instead of overlapping
+        it.  Off by default (the reference never clips).
     host_wait_timeout_s: bound on every host-side wait for another rank
         (optimizer publication, cpu_reduce slots); expiry raises TimeoutError.
     trace_path: append one JSON line per training step with per-phase
@@ -96,6 +104,7 @@ class SlideFSDPConfig:
     shard_source: str = "master"  # shard fetch reads the fp32 "master" (cast on GPU) or the bf16 "shadow"
     host_threads: int = 0
     host_wait_timeout_s: float = 600.0  # bound on every host wait for a peer rank
+    exact_grad_clip: bool = False  # clip to clip_grad_norm before the updates
     master_layout: str = "split"  # "split" (hi/lo 16-bit planes), "fp32" (fp32 + bf16 shadow) or "bf16"
     optimizer_state_dtype: str = "fp32"  # LayerAdam m/v in host memory: "fp32" or "bf16"
     use_native_kernels: Optional[bool] = None  # None: native iff device is CUDA

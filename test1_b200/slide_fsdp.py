@@ -315,6 +315,12 @@ class SlideFSDP(nn.Module):
         self.tracer = PhaseTracer(self.device, trace, self.rank, self.world_size)
         self.completed_steps = 0
         self.stats: Dict[str, float] = {}
+        # exact gradient clipping: per-layer squared norms and the deferred
+        # updates of the current step
+        self._exact_clip = bool(config.exact_grad_clip and config.clip_grad_norm > 0)
+        self._clip_parts: Dict[int, float] = {}
+        self._deferred: Dict[int, tuple] = {}
+        self.last_grad_norm: Optional[float] = None
         self.h2d_bytes = 0
         self.position_embeddings = None
         self._closed = False
@@ -692,14 +698,30 @@ class SlideFSDP(nn.Module):
         shadow = (st.shadow[s:e] if (has_work and st.store.layout == "fp32" and self.dtype != torch.float32)
                   else None)
 
-        def run_update(grad=None):
+        def run_update(grad=None, coef=1.0):
             if has_work:
                 g = grad if grad is not None else st.grad_host
                 t0 = time.perf_counter()
-                opt.step_flat(st.idx, g, shadow=shadow, grad_scale=scale)
+                opt.step_flat(st.idx, g, shadow=shadow, grad_scale=scale * coef)
                 self.tracer.host("adam", st.idx, time.perf_counter() - t0)
             if e > s:  # only ranks that own a slice publish
                 self.updates.publish(st.idx)
+
+        if self._exact_clip:
+            # measure now, update once the global norm is known
+            def measure(grad=None):
+                g = grad if grad is not None else st.grad_host
+                sq = 0.0
+                if has_work and g is not None and g.numel():
+                    sq = _native.host().sumsq(g) * scale * scale
+                self._clip_parts[st.idx] = sq
+                self._deferred[st.idx] = (run_update, grad)
+
+            if self._reducer is not None:
+                self._reducer.submit(st.idx, ready, lambda: measure(self.comm.host_reduce(st, step)))
+            else:
+                self.updates.submit(st.idx, ready, measure)
+            return
 
         if self._reducer is not None:
             def run_reduce():
@@ -849,11 +871,33 @@ class SlideFSDP(nn.Module):
             emb.module.backward_ids(dh, ctx.input_ids)
         del dh
         self._offload_grads(emb, step)
+        if self._exact_clip:
+            self._apply_exact_clip()
         self.acts.clear()
         self.completed_steps = step
         if self.tracer.enabled:
             self.tracer.step_done(step, {"h2d_bytes": self.h2d_bytes})
         return loss
+
+    def _apply_exact_clip(self) -> None:
+        """Every layer's gradient is on the host and measured: combine the
+        squared norms over ranks, then start the deferred updates with the
+        clip coefficient min(1, clip_grad_norm / (norm + 1e-6)) folded into
+        their gradient scale (lowest layer first, as the next forward needs
+        it first)."""
+        if self._reducer is not None:
+            self._reducer.drain()
+        self.updates.drain()
+        t = torch.tensor([sum(self._clip_parts.values())], dtype=torch.float64, device=self.device)
+        if self.world_size > 1 and not self.comm.rank0_optimizer:
+            dist.all_reduce(t)
+        norm = math.sqrt(float(t.item()))
+        coef = min(1.0, self.config.clip_grad_norm / (norm + 1e-6))
+        self.last_grad_norm = norm
+        deferred, self._deferred, self._clip_parts = self._deferred, {}, {}
+        for idx in sorted(deferred):
+            fn, g = deferred[idx]
+            self.updates.submit(idx, None, lambda fn=fn, g=g: fn(g, coef))
 
     @torch.no_grad()
     def _inference(self, input_ids: torch.Tensor) -> torch.Tensor:

@@ -17,7 +17,7 @@ def batches(cfg, world, steps, batch=2, seq=32):
             for _ in range(steps)]
 
 
-def run_engine(rank, world, port, mode, grad, sharding, steps, out_path, ckpt):
+def run_engine(rank, world, port, mode, grad, sharding, steps, out_path, ckpt, extra=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["LOCAL_WORLD_SIZE"] = str(world)
@@ -36,7 +36,8 @@ def run_engine(rank, world, port, mode, grad, sharding, steps, out_path, ckpt):
         model = LlamaForCausalLM(cfg)
         conf = SlideFSDPConfig(dtype=torch.float32, device="cpu", lr=1e-3, weight_decay=0.01,
                                param_transfer_mode=mode, grad_sync_mode=grad,
-                               optimizer_sharding=sharding, enable_activation_checkpoint=ckpt)
+                               optimizer_sharding=sharding, enable_activation_checkpoint=ckpt,
+                               **(extra or {}))
         eng = SlideFSDP(model, conf)
         losses = []
         for step_batches in batches(cfg, world, steps):
@@ -46,7 +47,7 @@ def run_engine(rank, world, port, mode, grad, sharding, steps, out_path, ckpt):
         dist.barrier()
         if rank == 0:
             master = {n: t.clone() for n, t in eng.named_master_tensors()}
-            torch.save({"losses": losses, "master": master}, out_path)
+            torch.save({"losses": losses, "master": master, "grad_norm": eng.last_grad_norm}, out_path)
         else:
             torch.save({"losses": losses}, out_path + f".{rank}")
         dist.barrier()

@@ -19,7 +19,7 @@ def _free_port():
     return port
 
 
-def _oracle(world, steps):
+def _oracle(world, steps, clip=None, eps=1e-8):
     import transformers
 
     from test1_b200.models.llama import LlamaConfig, LlamaForCausalLM
@@ -30,8 +30,8 @@ def _oracle(world, steps):
     hf = transformers.LlamaForCausalLM(cfg.to_hf()).float()
     hf.config._attn_implementation = "eager"
     hf.load_state_dict({n: p.detach().clone() for n, p in ours.named_parameters()})
-    opt = torch.optim.AdamW(hf.parameters(), lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01)
-    losses = []
+    opt = torch.optim.AdamW(hf.parameters(), lr=1e-3, betas=(0.9, 0.999), eps=eps, weight_decay=0.01)
+    losses, norms = [], []
     for step_batches in batches(cfg, world, steps):
         opt.zero_grad()
         per_rank = []
@@ -39,8 +39,12 @@ def _oracle(world, steps):
             loss = hf(input_ids=ids, labels=ids).loss / world
             loss.backward()
             per_rank.append(float(loss) * world)
+        if clip is not None:
+            norms.append(float(torch.nn.utils.clip_grad_norm_(hf.parameters(), clip)))
         opt.step()
         losses.append(per_rank)
+    if clip is not None:
+        return losses, dict(hf.named_parameters()), norms
     return losses, dict(hf.named_parameters())
 
 
@@ -108,3 +112,38 @@ def test_many_rank_engine_matches_oracle(tmp_path, world, mode, grad):
         d = (m - p.detach()).abs()
         assert (d > 1e-4).float().mean().item() < 1e-3, n
         assert d.max().item() < steps * 2 * 1e-3, n
+
+
+@pytest.mark.parametrize("mode,grad,sharding", [("full", "cpu_reduce", "rank"), ("shard", "gpu_reduce", "rank"),
+                                                ("full", "gpu_reduce", "rank0")])
+def test_two_rank_exact_grad_clip_matches_oracle(tmp_path, mode, grad, sharding):
+    """exact_grad_clip: the mean gradient over both ranks is clipped to the
+    global norm before any update, as clip_grad_norm_ + AdamW.step.  A large
+    eps makes Adam's step proportional to the gradient, so an unclipped (or
+    wrongly scaled) update lands far from the oracle."""
+    world, steps, clip, eps = 2, 3, 0.05, 1e-2
+    out = str(tmp_path / "res.pt")
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    extra = {"exact_grad_clip": True, "clip_grad_norm": clip, "adam_eps": eps}
+    procs = [ctx.Process(target=run_engine, args=(r, world, port, mode, grad, sharding, steps, out, True, extra))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    errs = [f for f in os.listdir(tmp_path) if ".err" in f]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    res0 = torch.load(out)
+    oracle_losses, oracle_params, norms = _oracle(world, steps, clip=clip, eps=eps)
+    _, unclipped = _oracle(world, steps, eps=eps)
+    assert norms[-1] > 10 * clip  # the clip was active
+    assert abs(res0["grad_norm"] - norms[-1]) < 1e-4 * norms[-1]
+    for s in range(steps):
+        assert abs(res0["losses"][s] - oracle_losses[s][0]) < 1e-4
+    far = 0.0
+    for n, p in oracle_params.items():
+        m = res0["master"][n].view(p.shape)
+        assert (m - p.detach()).abs().max().item() < 1e-5, n
+        far = max(far, (m - unclipped[n].detach()).abs().max().item())
+    assert far > 1e-4  # the test tells a clipped run from an unclipped one

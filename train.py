@@ -166,8 +166,10 @@ def main(argv=None):
                     t_start = time.perf_counter()
                 n = max(1, config.log_every_n_steps)
                 if rank == 0:
+                    gn = getattr(engine, "last_grad_norm", None)
+                    gn = f" | grad norm {gn:.4f}" if gn is not None else ""
                     print(f"Epoch {epoch} | Step {step} | Loss: {running / n:.4f} | "
-                          f"{tokens_per_step * n / dt:.1f} tokens/s | {flops * n / dt / 1e12:.2f} TFLOPS",
+                          f"{tokens_per_step * n / dt:.1f} tokens/s | {flops * n / dt / 1e12:.2f} TFLOPS{gn}",
                           flush=True)
                 running = 0.0
             if args.max_steps and step >= args.max_steps:
