@@ -52,21 +52,41 @@ def parse_args():
     p.add_argument("--baseline-config", type=int, default=2, choices=[2, 3, 4],
                    help="comparison config preset: 2 = 8B full + gpu_reduce, batch 4 x 1024 (default); "
                         "3 = 8B shard + gpu_reduce, AC cpu, batch 2 x 4096; 4 = 70B shard + cpu_reduce, "
-                        "bf16 weights and Adam state in host RAM, batch 1 x 2048")
+                        "batch 1 x 2048, bf16 weights and Adam state in host RAM (fp32 with >= 1.2 TB)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--profile-json", default="")
     args = p.parse_args()
     given = {a.split("=")[0] for a in sys.argv[1:] if a.startswith("--")}
-    presets = {
-        3: dict(model="llama31_8b", param_transfer_mode="shard", grad_sync_mode="gpu_reduce",
-                batch=2, seq=4096, ac_offload="cpu"),
-        4: dict(model="llama_70b", param_transfer_mode="shard", grad_sync_mode="cpu_reduce",
-                batch=1, seq=2048, ac_offload="cpu", master_layout="bf16", state_dtype="bf16"),
-    }
-    for k, v in presets.get(args.baseline_config, {}).items():
+    for k, v in baseline_preset(args.baseline_config, host_ram_bytes()).items():
         if "--" + k.replace("_", "-") not in given:  # explicit flags win
             setattr(args, k, v)
     return args
+
+
+def host_ram_bytes() -> int:
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemTotal:"):
+                    return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return 0
+
+
+def baseline_preset(cfg: int, ram_bytes: int) -> dict:
+    """Flag values of comparison configs 3 and 4.  Config 4 (70B) keeps an
+    fp32 master and fp32 Adam state when the host has at least 1.2 TB of RAM
+    (about 1.1 TB of host state), else bf16 weights and bf16 state."""
+    if cfg == 3:
+        return dict(model="llama31_8b", param_transfer_mode="shard", grad_sync_mode="gpu_reduce",
+                    batch=2, seq=4096, ac_offload="cpu")
+    if cfg == 4:
+        big = ram_bytes >= 1.2e12
+        return dict(model="llama_70b", param_transfer_mode="shard", grad_sync_mode="cpu_reduce",
+                    batch=1, seq=2048, ac_offload="cpu", master_layout="split" if big else "bf16",
+                    state_dtype="fp32" if big else "bf16")
+    return {}
 
 
 class ClockSampler:

@@ -127,3 +127,19 @@ def test_native_loader_selects_the_bounds_checked_build(monkeypatch):
     assert _native.cuda() == "_cuda_checked"
     monkeypatch.setenv("T1_BOUNDS_CHECK", "0")
     assert _native.cuda() == "_cuda"
+
+
+def test_bench_presets_follow_host_ram():
+    import importlib.util
+    import os
+
+    spec = importlib.util.spec_from_file_location(
+        "bench_mod", os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    small = bench.baseline_preset(4, 512 * 2**30)
+    assert small["master_layout"] == "bf16" and small["state_dtype"] == "bf16"
+    big = bench.baseline_preset(4, 2 * 10**12)
+    assert big["master_layout"] == "split" and big["state_dtype"] == "fp32"
+    assert bench.baseline_preset(3, 0)["seq"] == 4096 and bench.baseline_preset(2, 0) == {}
+    assert bench.host_ram_bytes() > 0
