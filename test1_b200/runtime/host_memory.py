@@ -39,6 +39,29 @@ def _align(x: int, a: int = ALIGN_BYTES) -> int:
     return (x + a - 1) // a * a
 
 
+def mem_available_bytes() -> Optional[int]:
+    """The kernel's estimate of memory available to new allocations
+    (MemAvailable), or None where /proc/meminfo does not say."""
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemAvailable:"):
+                    return int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    return None
+
+
+def shm_free_bytes(path: str = "/dev/shm") -> Optional[int]:
+    """Free space of the shared-memory mount (a file larger than it faults
+    with SIGBUS on first touch instead of failing at creation)."""
+    try:
+        st = os.statvfs(path)
+    except OSError:
+        return None
+    return st.f_bavail * st.f_frsize
+
+
 def _checksum(words: List[int]) -> int:
     c = 0x9E3779B97F4A7C15
     for w in words:

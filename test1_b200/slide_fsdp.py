@@ -55,6 +55,7 @@ from .optim.layer_adam import LayerAdam
 from .parallel.comm import CpuReduceSlots, make_comm
 from .runtime.activations import ActivationStore
 from .runtime.device import Event, Stream
+from .runtime import host_memory
 from .runtime.host_memory import (REGION_HEADER_BYTES, HostRegion, MasterStore, RegionPlanner,
                                   check_region_header, write_region_header)
 from .utils.trace import PhaseTracer
@@ -214,6 +215,7 @@ class SlideFSDP(nn.Module):
         shm_path = None
         if self.world_size > 1:
             shm_path = f"/dev/shm/t1b200_{self._session}.bin"
+        self._check_host_capacity(plan.size, shm_path)
         creator = self.rank == 0
         if self.world_size > 1 and not creator:
             dist.barrier()
@@ -357,6 +359,41 @@ class SlideFSDP(nn.Module):
             else:
                 merged.append([a, b])
         return [(a, b - a) for a, b in merged]
+
+    def _check_host_capacity(self, shared_bytes: int, shm_path: Optional[str]) -> None:
+        """Refuse, on every rank alike and before anything is allocated, a
+        configuration whose host memory does not fit this node: an
+        over-committed node kills ranks (or its other jobs) in the middle of
+        a run, and a shared-memory file larger than its mount faults on
+        first touch.  Counts the shared master, every local rank's gradient
+        shards and optimizer state."""
+        c = self.config
+        local = int(os.environ.get("LOCAL_WORLD_SIZE", str(self.world_size)) or 1)
+        es = torch.tensor([], dtype=self.dtype).element_size()
+        sb = 2 if c.optimizer_state_dtype == "bf16" else 4
+        if self.world_size > 1 and c.optimizer_sharding == "rank0":
+            owned = self.total_params  # one optimizer and gradient copy on the node
+        else:
+            owned = self.total_params * min(local, self.world_size) / self.world_size
+        need = shared_bytes + owned * (2 * sb + es)
+        avail = host_memory.mem_available_bytes()
+        problems = []
+        if avail is not None and need > avail:
+            problems.append(f"host memory: {need / 1e9:.1f} GB needed (master {shared_bytes / 1e9:.1f} GB, "
+                            f"optimizer state and gradients {owned * (2 * sb + es) / 1e9:.1f} GB for "
+                            f"{min(local, self.world_size)} local rank(s)), {avail / 1e9:.1f} GB available")
+        if shm_path is not None:
+            free = host_memory.shm_free_bytes(os.path.dirname(shm_path))
+            if free is not None and shared_bytes > free:
+                problems.append(f"{os.path.dirname(shm_path)}: {shared_bytes / 1e9:.1f} GB needed, "
+                                f"{free / 1e9:.1f} GB free")
+        bad = torch.tensor([1.0 if problems else 0.0], device=self.device)
+        if self.world_size > 1:
+            dist.all_reduce(bad, op=dist.ReduceOp.MAX)
+        if bad.item() > 0:
+            detail = "; ".join(problems) if problems else "another rank found too little host memory"
+            raise MemoryError(f"rank {self.rank}: this model and configuration do not fit on the node: {detail} "
+                              f"(bf16 optimizer state, master_layout='bf16' or more nodes reduce it)")
 
     def _region_fields(self, nbytes: int) -> dict:
         """What the shared region's layout depends on, for its header."""

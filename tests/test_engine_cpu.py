@@ -164,3 +164,11 @@ def test_out_of_range_token_ids_and_labels_are_rejected():
         assert torch.isfinite(eng(input_ids=ids, labels=lab).loss)
     finally:
         eng.close()
+
+
+def test_configuration_larger_than_host_memory_is_refused(monkeypatch):
+    from test1_b200.runtime import host_memory
+
+    monkeypatch.setattr(host_memory, "mem_available_bytes", lambda: 1 << 20)
+    with pytest.raises(MemoryError, match="do not fit on the node: host memory"):
+        SlideFSDP(LlamaForCausalLM(LlamaConfig.tiny()), SlideFSDPConfig(dtype=torch.float32, device="cpu"))
