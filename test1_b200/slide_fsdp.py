@@ -1062,26 +1062,60 @@ class SlideFSDP(nn.Module):
             dist.barrier()
 
     def load_state(self, directory: str) -> None:
+        """Restore a ``save_state`` directory.  The world size and optimizer
+        placement may differ from the saving run's: each rank assembles its
+        own shard of every layer's optimizer state from the saved shards that
+        overlap it (read through memory maps, so only those bytes are
+        read), which lets a run resume on another number of GPUs."""
         self.wait_for_updates()
         with open(os.path.join(directory, "manifest.json")) as f:
             manifest = json.load(f)
-        if manifest["world_size"] != self.world_size:
-            raise ValueError("optimizer shards were saved with a different world size")
-        host = _native.host()
+        if manifest["num_layers"] != self.num_layers:
+            raise ValueError(f"the saved state has {manifest['num_layers']} layers, this model {self.num_layers}")
         if self.rank == 0:
             for st in self.layer_states:
                 st.store.write_fp32(torch.load(os.path.join(directory, f"layer_{st.idx}.pt")))
         if self.layer_optimizer is not None:
+            saved_world = int(manifest["world_size"])
             for st in self.layer_states:
                 if st.shard[1] > st.shard[0]:
-                    sd = torch.load(os.path.join(directory, f"optim_rank{self.rank}_layer_{st.idx}.pt"))
-                    if tuple(sd["shard"]) != tuple(st.shard):
-                        raise ValueError(f"shard mismatch for layer {st.idx}")
+                    sd = self._assemble_optimizer_shard(directory, st, saved_world)
                     self.layer_optimizer.load_state_for_layer(st.idx, sd)
         # counters keep counting from here: completed_steps is the number of
         # update rounds already published by this process group
         if self.world_size > 1:
             dist.barrier()
+
+    def _assemble_optimizer_shard(self, directory: str, st: LayerRuntimeState, saved_world: int) -> dict:
+        """m, v and step of this rank's range [s, e) of layer ``st`` from the
+        saved per-rank files, whatever ranges they cover."""
+        s, e = st.shard
+        out = None
+        covered = 0
+        step = None
+        for r in range(saved_world):
+            path = os.path.join(directory, f"optim_rank{r}_layer_{st.idx}.pt")
+            if not os.path.exists(path):
+                continue  # that rank owned nothing of this layer
+            sd = torch.load(path, mmap=True)
+            a, b = (int(x) for x in sd["shard"])
+            lo, hi = max(a, s), min(b, e)
+            if step is not None and int(sd["step"]) != step:
+                raise ValueError(f"layer {st.idx}: saved shards disagree on the step count")
+            step = int(sd["step"])
+            if hi <= lo:
+                continue
+            if out is None:
+                out = {"exp_avg": torch.empty(e - s, dtype=sd["exp_avg"].dtype),
+                       "exp_avg_sq": torch.empty(e - s, dtype=sd["exp_avg_sq"].dtype)}
+            for k in ("exp_avg", "exp_avg_sq"):
+                out[k][lo - s:hi - s].copy_(sd[k][lo - a:hi - a])
+            covered += hi - lo
+        if out is None or covered != e - s:
+            raise ValueError(f"layer {st.idx}: the saved optimizer shards cover {covered} of the "
+                             f"{e - s} elements this rank needs")
+        out["step"] = step
+        return out
 
     # --------------------------------------------------------------- misc
     def step_stats(self) -> Dict[str, float]:

@@ -57,3 +57,37 @@ def run_engine(rank, world, port, mode, grad, sharding, steps, out_path, ckpt, e
         with open(out_path + f".err{rank}", "w") as f:
             f.write(traceback.format_exc())
         raise
+
+
+def run_state(rank, world, port, sharding, load_dir, save_dir, steps, err_path):
+    """Optionally load a saved state, train ``steps`` steps (2 x 32 tokens
+    per rank), then save the state."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["LOCAL_WORLD_SIZE"] = str(world)
+    os.environ["LOCAL_RANK"] = str(rank)
+    os.environ["T1_QUIET"] = "1"
+    try:
+        from datetime import timedelta
+
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+        from test1_b200 import SlideFSDPConfig
+        from test1_b200.models.llama import LlamaConfig, LlamaForCausalLM
+        from test1_b200.slide_fsdp import SlideFSDP
+
+        cfg = LlamaConfig.tiny()
+        torch.manual_seed(0)
+        eng = SlideFSDP(LlamaForCausalLM(cfg), SlideFSDPConfig(dtype=torch.float32, device="cpu", lr=1e-3,
+                                                               optimizer_sharding=sharding))
+        if load_dir:
+            eng.load_state(load_dir)
+        for step_batches in batches(cfg, world, steps):
+            ids = step_batches[rank]
+            eng(input_ids=ids, labels=ids)
+        eng.save_state(save_dir)
+        eng.close()
+        dist.destroy_process_group()
+    except Exception:
+        with open(err_path + f".err{rank}", "w") as f:
+            f.write(traceback.format_exc())
+        raise

@@ -1,5 +1,7 @@
 """save_pretrained writes a directory HF transformers loads with identical
-outputs; save_state/load_state resume is bit-exact."""
+outputs; save_state/load_state resume is bit-exact, also on another world
+size."""
+import pytest
 import torch
 
 from test1_b200 import SlideFSDPConfig
@@ -58,3 +60,68 @@ def test_save_state_resume_bit_exact(tmp_path):
     c.close()
     for n, t in ref.items():
         assert torch.equal(got[n], t), n
+
+
+def _run_ranks(world, sharding, load_dir, save_dir, steps, tmp_path):
+    import os
+    import socket
+
+    import torch.multiprocessing as mp
+
+    from tests._dist_worker import run_state
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    err = str(tmp_path / f"state_{world}")
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=run_state, args=(r, world, port, sharding, load_dir, save_dir, steps, err))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    errs = [f for f in os.listdir(tmp_path) if ".err" in f]
+    assert not errs, open(os.path.join(tmp_path, errs[0])).read()
+    assert all(p.exitcode == 0 for p in procs)
+
+
+def _full_optimizer_state(directory, layer, world):
+    import os
+
+    parts = []
+    for r in range(world):
+        path = os.path.join(directory, f"optim_rank{r}_layer_{layer}.pt")
+        if os.path.exists(path):
+            sd = torch.load(path)
+            parts.append((int(sd["shard"][0]), sd["exp_avg"], sd["exp_avg_sq"], int(sd["step"])))
+    parts.sort(key=lambda x: x[0])
+    return (torch.cat([p[1] for p in parts]), torch.cat([p[2] for p in parts]), {p[3] for p in parts})
+
+
+@pytest.mark.parametrize("world_a,world_b,sharding_b", [(2, 1, "rank"), (2, 4, "rank"), (2, 2, "rank0")])
+def test_state_saved_at_one_world_size_resumes_at_another(tmp_path, world_a, world_b, sharding_b):
+    """Optimizer shards saved by world_a ranks are re-cut for world_b ranks
+    (or for a rank-0 optimizer) on load: saving again right after loading
+    gives back the same full master and the same full m, v and steps."""
+    import os
+
+    a, b = str(tmp_path / "a"), str(tmp_path / "b")
+    _run_ranks(world_a, "rank", None, a, 2, tmp_path)
+    if world_b == 1:
+        torch.manual_seed(0)
+        eng = SlideFSDP(LlamaForCausalLM(LlamaConfig.tiny()),
+                        SlideFSDPConfig(dtype=torch.float32, device="cpu", lr=1e-3))
+        eng.load_state(a)
+        eng.save_state(b)
+        eng.close()
+    else:
+        _run_ranks(world_b, sharding_b, a, b, 0, tmp_path)
+    n_layers = LlamaConfig.tiny().num_hidden_layers + 2
+    for i in range(n_layers):
+        assert torch.equal(torch.load(os.path.join(a, f"layer_{i}.pt")), torch.load(os.path.join(b, f"layer_{i}.pt")))
+        ma, va, sa = _full_optimizer_state(a, i, world_a)
+        mb, vb, sb = _full_optimizer_state(b, i, world_b)
+        assert torch.equal(ma, mb) and torch.equal(va, vb), i
+        assert sa == sb == {2}, (sa, sb)
