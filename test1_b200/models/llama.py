@@ -1,4 +1,8 @@
 """Llama-architecture causal LM with explicit per-layer forward/backward.
+The reference runs HF's modules under autograd, one checkpointed layer at a
+time (slide_fsdp.py:546-640, model loaded in train.py:94-123); here each
+decoder layer is a fixed program of sm_100a kernels with a hand-written
+backward.
 
 Parameter names and ``named_parameters()`` order match HuggingFace's
 ``LlamaForCausalLM`` (model.embed_tokens, model.layers.{i}.self_attn.{q,k,v,o}_proj,

@@ -1,4 +1,6 @@
-"""Plain-PyTorch statements of every op of the Llama training step.
+"""Plain-PyTorch statements of every op of the Llama training step (the
+reference computes them with HF / Liger modules; its loss is Liger's fused
+linear cross-entropy or nn.CrossEntropyLoss, slide_fsdp.py:87-109).
 
 These are the numerics oracle for the sm_100a kernels (tests compare each
 kernel against the function of the same name here, computed in fp32) and the

@@ -1,5 +1,8 @@
 """Fused NVLink communication for the sliding engine (one process per GPU,
-all GPUs of one node).
+all GPUs of one node).  It replaces the reference's shard all-gather
+(distributed_sync.py:118-158) and gpu_reduce gradient reduction
+(distributed_sync.py:242-300, reduce to rank 0 + D2H) with kernels that move
+the data over peer memory themselves.
 
 The pool units live in symmetric memory (``torch.distributed._symmetric_memory``:
 one allocation per buffer, mapped into every rank, plus a per-buffer signal

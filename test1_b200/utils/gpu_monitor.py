@@ -1,6 +1,8 @@
 """Background sampler of GPU utilisation, SM clock and memory through NVML
 (nvidia-ml-py), with throttle reasons.  Read-only: it never changes a GPU
-setting."""
+setting.  The reference's monitor (utils/gpu_monitor.py:6-75) samples
+utilisation only and is never started; this one feeds the bench's clock
+record."""
 from __future__ import annotations
 
 import statistics

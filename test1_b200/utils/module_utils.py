@@ -1,4 +1,5 @@
-"""Readable module tree with parameter counts."""
+"""Readable module tree with parameter counts (the reference's recursive
+printer, utils/module_utils.py:3-30, prints names only)."""
 from __future__ import annotations
 
 import torch.nn as nn

@@ -1,4 +1,5 @@
-"""Per-layer, per-operation timing with CUDA events (no host sync until read).
+"""Per-layer, per-operation timing with CUDA events (no host sync until read;
+the reference's LayerTimer, utils/timer.py:4-29, uses host clocks).
 
     t = LayerTimer(); t.start(3, "h2d"); ...; t.stop(3, "h2d"); t.summary()
 """
