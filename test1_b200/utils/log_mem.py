@@ -1,5 +1,5 @@
 """One-line device memory report (allocated / reserved / peak) for logs
-(the reference's utils/log_mem.py:5-14 reports allocated / reserved)."""
+(the figures of the reference's utils/log_mem.py:5-14)."""
 from __future__ import annotations
 
 import torch

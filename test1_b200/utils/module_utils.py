@@ -1,5 +1,5 @@
 """Readable module tree with parameter counts (the reference's recursive
-printer, utils/module_utils.py:3-30, prints names only)."""
+printer, utils/module_utils.py:3-30, shows each module's device and dtype)."""
 from __future__ import annotations
 
 import torch.nn as nn

@@ -1,5 +1,6 @@
 """Per-layer, per-operation timing with CUDA events (no host sync until read;
-the reference's LayerTimer, utils/timer.py:4-29, uses host clocks).
+the reference's LayerTimer, utils/timer.py:4-29, stores durations its caller
+measured).
 
     t = LayerTimer(); t.start(3, "h2d"); ...; t.stop(3, "h2d"); t.summary()
 """
