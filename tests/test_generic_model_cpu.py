@@ -101,3 +101,31 @@ def test_train_cli_runs_a_non_llama_checkpoint(tmp_path):
                        capture_output=True, text=True, timeout=600, cwd=root)
     assert r.returncode == 0, r.stderr[-2000:]
     assert "Model type: qwen2" in r.stdout and "Training completed" in r.stdout
+
+
+def test_generic_exact_grad_clip_matches_hf():
+    """One process: the global norm over every layer (biases included) is
+    clipped before the updates, as clip_grad_norm_ + AdamW.step."""
+    clip, eps = 0.05, 1e-2
+    model = _tiny_qwen2()
+    oracle = _tiny_qwen2()
+    oracle.load_state_dict(model.state_dict())
+    opt = torch.optim.AdamW(oracle.parameters(), lr=1e-3, eps=eps, weight_decay=0.01)
+    eng = SlideFSDP(model, SlideFSDPConfig(dtype=torch.float32, device="cpu", lr=1e-3, weight_decay=0.01,
+                                           adam_eps=eps, exact_grad_clip=True, clip_grad_norm=clip))
+    g = torch.Generator().manual_seed(3)
+    try:
+        for _ in range(3):
+            ids = torch.randint(0, 256, (2, 32), generator=g)
+            eng(input_ids=ids, labels=ids)
+            opt.zero_grad()
+            oracle(input_ids=ids, labels=ids).loss.backward()
+            norm = float(torch.nn.utils.clip_grad_norm_(oracle.parameters(), clip))
+            opt.step()
+            eng.wait_for_updates()
+            assert norm > 10 * clip and abs(eng.last_grad_norm - norm) < 1e-4 * norm
+        master = dict(eng.named_master_tensors())
+        for n, p in oracle.named_parameters():
+            assert (master[n].view(p.shape) - p.detach()).abs().max().item() < 1e-5, n
+    finally:
+        eng.close()
