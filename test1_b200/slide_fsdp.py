@@ -39,6 +39,7 @@ import math
 import os
 import time
 import uuid
+import warnings
 import zlib
 from dataclasses import dataclass
 from typing import Dict, List, Optional
@@ -1129,8 +1130,8 @@ class SlideFSDP(nn.Module):
         self._closed = True
         try:
             self.wait_for_updates()
-        except Exception:
-            pass
+        except Exception as exc:  # closing still releases everything; say what was lost
+            warnings.warn(f"SlideFSDP.close: pending optimizer updates did not complete: {exc}")
         self.updates.close()
         if self._reducer is not None:
             self._reducer.close()
