@@ -125,3 +125,23 @@ def test_state_saved_at_one_world_size_resumes_at_another(tmp_path, world_a, wor
         mb, vb, sb = _full_optimizer_state(b, i, world_b)
         assert torch.equal(ma, mb) and torch.equal(va, vb), i
         assert sa == sb == {2}, (sa, sb)
+
+
+def test_train_cli_periodic_state_and_resume(tmp_path):
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = str(tmp_path / "out")
+    base = [sys.executable, os.path.join(root, "train.py"), "--model-config", "tiny", "--device", "cpu",
+            "--batch-size", "2", "--seq-length", "32", "--num-epochs", "1", "--output-dir", out]
+    r = subprocess.run(base + ["--max-steps", "6", "--save-state-every", "2"], capture_output=True, text=True,
+                       timeout=600, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert open(os.path.join(out, "latest_state")).read() == "state_step6"
+    assert sorted(d for d in os.listdir(out) if d.startswith("state_step")) == ["state_step4", "state_step6"]
+    r = subprocess.run(base + ["--max-steps", "1", "--resume", out], capture_output=True, text=True,
+                       timeout=600, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "Resumed from" in r.stdout and "state_step6" in r.stdout

@@ -41,7 +41,12 @@ def parse_args(argv=None):
     p.add_argument("--output-dir", type=str, default="./output")
     p.add_argument("--save-model", action="store_true")
     p.add_argument("--save-state", action="store_true", help="also save master + optimizer state")
-    p.add_argument("--resume", type=str, default=None, help="directory written by --save-state")
+    p.add_argument("--save-state-every", type=int, default=0,
+                   help="also save master + optimizer state every N steps (output_dir/state_step<N>; "
+                        "the two newest are kept, output_dir/latest_state names the newest)")
+    p.add_argument("--resume", type=str, default=None,
+                   help="directory written by --save-state / --save-state-every, or an output_dir "
+                        "holding latest_state (the world size may differ from the saving run's)")
     p.add_argument("--seed", type=int, default=42)
     p.add_argument("--device", type=str, default=None, help="override device (e.g. cpu)")
     return p.parse_args(argv)
@@ -127,7 +132,14 @@ def main(argv=None):
     flops = calculate_flops_per_batch(mcfg, config.train_batch_size, config.max_seq_length) * world
     engine = SlideFSDP(model, config)
     if args.resume:
-        engine.load_state(args.resume)
+        src = args.resume
+        marker = os.path.join(src, "latest_state")
+        if os.path.isfile(marker):
+            with open(marker) as f:
+                src = os.path.join(src, f.read().strip())
+        engine.load_state(src)
+        if rank == 0:
+            print(f"Resumed from {src}", flush=True)
 
     from torch.utils.data import DataLoader
     from torch.utils.data.distributed import DistributedSampler
@@ -172,6 +184,8 @@ def main(argv=None):
                           f"{tokens_per_step * n / dt:.1f} tokens/s | {flops * n / dt / 1e12:.2f} TFLOPS{gn}",
                           flush=True)
                 running = 0.0
+            if args.save_state_every and step % args.save_state_every == 0:
+                save_periodic_state(engine, args.output_dir, step, rank, world)
             if args.max_steps and step >= args.max_steps:
                 break
         if args.max_steps and step >= args.max_steps:
@@ -189,6 +203,30 @@ def main(argv=None):
         dist.destroy_process_group()
     if rank == 0:
         print("Training completed!")
+
+
+def save_periodic_state(engine, output_dir: str, step: int, rank: int, world: int) -> None:
+    """Save the full training state into output_dir/state_step<step>; once
+    every rank has written its part, rank 0 points latest_state at it and
+    drops all but the two newest such directories, so a crash during a save
+    always leaves a complete earlier one."""
+    import shutil
+
+    name = f"state_step{step}"
+    engine.save_state(os.path.join(output_dir, name))  # ends with a barrier on every rank
+    if rank == 0:
+        tmp = os.path.join(output_dir, "latest_state.tmp")
+        with open(tmp, "w") as f:
+            f.write(name)
+        os.replace(tmp, os.path.join(output_dir, "latest_state"))
+        old = sorted((d for d in os.listdir(output_dir) if d.startswith("state_step") and d[10:].isdigit()),
+                     key=lambda d: int(d[10:]))
+        for d in old[:-2]:
+            shutil.rmtree(os.path.join(output_dir, d), ignore_errors=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
 
 
 if __name__ == "__main__":
