@@ -281,12 +281,27 @@ static void sum_slots_kernel(const void* const* srcs, int nsrc, void* dst, float
   const typename V::R sc = V::set1(scale);
   constexpr int W = V::W;
   int64_t i = b;
+  // The destination is only written: streaming stores skip the
+  // read-for-ownership that a cached store costs (a quarter of the traffic
+  // with two sources).  Elements up to the first vector-aligned one go
+  // through the scalar path.
+  while (i < e && !V::template can_stream<DDT>(d + i) && i - b < W) {
+    float acc = 0.0f;
+    for (int k = 0; k < nsrc; ++k) acc += Elem<SDT>::ld(static_cast<const STy*>(srcs[k]) + i);
+    Elem<DDT>::st(d + i, acc * scale);
+    ++i;
+  }
+  const bool nt = i < e && V::template can_stream<DDT>(d + i);
   for (; i + W <= e; i += W) {
     typename V::R acc = V::zero();
     for (int k = 0; k < nsrc; ++k)
       acc = V::add(acc, V::template ld<SDT>(static_cast<const STy*>(srcs[k]) + i));
-    V::template st<DDT>(d + i, V::mul(acc, sc));
+    if (nt)
+      V::template st_stream<DDT>(d + i, V::mul(acc, sc));
+    else
+      V::template st<DDT>(d + i, V::mul(acc, sc));
   }
+  if (nt) V::fence();
   for (; i < e; ++i) {
     float acc = 0.0f;
     for (int k = 0; k < nsrc; ++k) acc += Elem<SDT>::ld(static_cast<const STy*>(srcs[k]) + i);
