@@ -341,14 +341,18 @@ class LayerAdam:
 
     @torch.no_grad()
     def step_flat(self, layer_idx: int, grad: Optional[torch.Tensor],
-                  shadow: Optional[torch.Tensor] = None, grad_scale: float = 1.0) -> None:
+                  shadow: Optional[torch.Tensor] = None, grad_scale: float = 1.0,
+                  lr: Optional[float] = None) -> None:
         """Engine path: update the flat slice registered with
         ``add_flat_layer`` from ``grad`` (same numel, any float dtype; None =
         zero gradient), writing the low-precision ``shadow`` in the same
-        pass."""
+        pass.  ``lr`` overrides the group's learning rate for this update (the
+        engine passes the rate that was current when the step ran)."""
         group = self._group(layer_idx)
         self._pre_step(layer_idx)
         group["step"] += 1
+        if lr is not None:
+            group = dict(group, lr=lr)
         param = self._flat_param[layer_idx]
         if isinstance(param, tuple):
             beta1, beta2 = group["betas"]

@@ -733,6 +733,7 @@ class SlideFSDP(nn.Module):
         s, e = st.shard
         has_work = opt is not None and e > s
         scale = self.comm.grad_scale
+        lr = self.config.lr  # the rate of the step that produced these gradients
         shadow = (st.shadow[s:e] if (has_work and st.store.layout == "fp32" and self.dtype != torch.float32)
                   else None)
 
@@ -740,7 +741,7 @@ class SlideFSDP(nn.Module):
             if has_work:
                 g = grad if grad is not None else st.grad_host
                 t0 = time.perf_counter()
-                opt.step_flat(st.idx, g, shadow=shadow, grad_scale=scale * coef)
+                opt.step_flat(st.idx, g, shadow=shadow, grad_scale=scale * coef, lr=lr)
                 self.tracer.host("adam", st.idx, time.perf_counter() - t0)
             if e > s:  # only ranks that own a slice publish
                 self.updates.publish(st.idx)
@@ -972,7 +973,10 @@ class SlideFSDP(nn.Module):
             self.updates.wait_counter(st.idx, self._update_target(st))
 
     def update_learning_rate(self, new_lr: float) -> None:
-        self.wait_for_updates()
+        """Rate for the steps that start from now on.  Updates of earlier
+        steps still in flight keep the rate their step ran with (each update
+        carries it), so a per-step schedule costs no synchronisation: the
+        optimizer tail of one step keeps overlapping the next forward."""
         self.config.lr = new_lr
         if self.layer_optimizer is not None:
             self.layer_optimizer.update_learning_rate(new_lr)

@@ -172,3 +172,37 @@ def test_configuration_larger_than_host_memory_is_refused(monkeypatch):
     monkeypatch.setattr(host_memory, "mem_available_bytes", lambda: 1 << 20)
     with pytest.raises(MemoryError, match="do not fit on the node: host memory"):
         SlideFSDP(LlamaForCausalLM(LlamaConfig.tiny()), SlideFSDPConfig(dtype=torch.float32, device="cpu"))
+
+
+def test_per_step_learning_rate_schedule_matches_adamw():
+    """update_learning_rate between steps (no synchronisation): every update
+    uses the rate of the step that produced its gradient."""
+    import transformers
+
+    cfg = LlamaConfig.tiny()
+    torch.manual_seed(0)
+    ours = LlamaForCausalLM(cfg)
+    hf = transformers.LlamaForCausalLM(cfg.to_hf()).float()
+    hf.config._attn_implementation = "eager"
+    hf.load_state_dict({n: p.detach().clone() for n, p in ours.named_parameters()})
+    opt = torch.optim.AdamW(hf.parameters(), lr=1e-3, weight_decay=0.01)
+    eng = SlideFSDP(ours, SlideFSDPConfig(dtype=torch.float32, device="cpu", lr=1e-3, weight_decay=0.01))
+    g = torch.Generator().manual_seed(7)
+    try:
+        for lr in (1e-3, 3e-3, 2e-4, 5e-3):
+            ids = torch.randint(0, cfg.vocab_size, (2, 32), generator=g)
+            eng.update_learning_rate(lr)
+            eng(input_ids=ids, labels=ids)
+            for grp in opt.param_groups:
+                grp["lr"] = lr
+            opt.zero_grad()
+            hf(input_ids=ids, labels=ids).loss.backward()
+            opt.step()
+        eng.wait_for_updates()
+        master = dict(eng.named_master_tensors())
+        for n, p in hf.named_parameters():
+            d = (master[n].view(p.shape) - p.detach()).abs()
+            assert (d > 1e-4).float().mean().item() < 1e-3, n
+            assert d.max().item() < 4 * 5e-3, n
+    finally:
+        eng.close()
