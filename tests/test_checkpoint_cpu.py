@@ -145,3 +145,30 @@ def test_train_cli_periodic_state_and_resume(tmp_path):
                        timeout=600, cwd=root)
     assert r.returncode == 0, r.stderr[-2000:]
     assert "Resumed from" in r.stdout and "state_step6" in r.stdout
+
+
+def test_train_cli_learning_rate_schedule(tmp_path):
+    import importlib.util
+    import math
+    import os
+    import re
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("train_mod", os.path.join(root, "train.py"))
+    tm = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(tm)
+    assert tm.scheduled_lr(1.0, 0, 10, 2, "cosine") == 0.5
+    assert tm.scheduled_lr(1.0, 2, 10, 2, "cosine") == 1.0
+    assert abs(tm.scheduled_lr(1.0, 6, 10, 2, "cosine") - 0.5) < 1e-12
+    assert tm.scheduled_lr(1.0, 6, 10, 2, "linear") == 0.5
+    assert tm.scheduled_lr(1.0, 9, 10, 0, "constant") == 1.0
+    r = subprocess.run([sys.executable, os.path.join(root, "train.py"), "--model-config", "tiny", "--device", "cpu",
+                        "--batch-size", "2", "--seq-length", "32", "--num-epochs", "1", "--max-steps", "4",
+                        "--lr", "1e-3", "--lr-scheduler", "cosine", "--warmup-steps", "2",
+                        "--output-dir", str(tmp_path / "out")], capture_output=True, text=True, timeout=600, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lrs = [float(x) for x in re.findall(r"\| lr ([0-9.e+-]+)", r.stdout)]
+    want = [tm.scheduled_lr(1e-3, s, 4, 2, "cosine") for s in range(4)]
+    assert len(lrs) == 4 and all(math.isclose(a, b, rel_tol=1e-2) for a, b in zip(lrs, want)), (lrs, want)

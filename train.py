@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import random
 import sys
@@ -41,6 +42,9 @@ def parse_args(argv=None):
     p.add_argument("--output-dir", type=str, default="./output")
     p.add_argument("--save-model", action="store_true")
     p.add_argument("--save-state", action="store_true", help="also save master + optimizer state")
+    p.add_argument("--lr-scheduler", choices=["constant", "linear", "cosine"], default="constant",
+                   help="per-step learning-rate schedule after --warmup-steps of linear warm-up")
+    p.add_argument("--warmup-steps", type=int, default=0)
     p.add_argument("--save-state-every", type=int, default=0,
                    help="also save master + optimizer state every N steps (output_dir/state_step<N>; "
                         "the two newest are kept, output_dir/latest_state names the newest)")
@@ -150,6 +154,10 @@ def main(argv=None):
     loader = DataLoader(ds, batch_size=config.train_batch_size, sampler=sampler,
                         shuffle=sampler is None, drop_last=True, pin_memory=config.device.type == "cuda")
     tokens_per_step = config.train_batch_size * config.max_seq_length * world
+    total_steps = len(loader) * config.num_epochs
+    if args.max_steps:
+        total_steps = min(total_steps, args.max_steps)
+    base_lr = config.lr
     step = 0
     timed = config.device.type == "cuda"
     for epoch in range(1, config.num_epochs + 1):
@@ -161,6 +169,9 @@ def main(argv=None):
             ev0.record()
         running = 0.0
         for batch in loader:
+            if args.lr_scheduler != "constant" or args.warmup_steps:
+                engine.update_learning_rate(
+                    scheduled_lr(base_lr, step, total_steps, args.warmup_steps, args.lr_scheduler))
             batch = {k: v.to(config.device, non_blocking=True) for k, v in batch.items()}
             out = engine(input_ids=batch["input_ids"], attention_mask=batch["attention_mask"],
                          labels=batch["labels"])
@@ -181,7 +192,8 @@ def main(argv=None):
                     gn = getattr(engine, "last_grad_norm", None)
                     gn = f" | grad norm {gn:.4f}" if gn is not None else ""
                     print(f"Epoch {epoch} | Step {step} | Loss: {running / n:.4f} | "
-                          f"{tokens_per_step * n / dt:.1f} tokens/s | {flops * n / dt / 1e12:.2f} TFLOPS{gn}",
+                          f"{tokens_per_step * n / dt:.1f} tokens/s | {flops * n / dt / 1e12:.2f} TFLOPS | "
+                          f"lr {engine.config.lr:.3g}{gn}",
                           flush=True)
                 running = 0.0
             if args.save_state_every and step % args.save_state_every == 0:
@@ -203,6 +215,20 @@ def main(argv=None):
         dist.destroy_process_group()
     if rank == 0:
         print("Training completed!")
+
+
+def scheduled_lr(base: float, step: int, total: int, warmup: int, kind: str) -> float:
+    """Learning rate of step ``step`` (0-based): linear warm-up over
+    ``warmup`` steps, then constant, linear decay to 0, or half-cosine decay
+    to 0 at ``total`` steps."""
+    if warmup and step < warmup:
+        return base * (step + 1) / warmup
+    if kind == "constant" or total <= warmup:
+        return base
+    frac = min(1.0, (step - warmup) / max(1, total - warmup))
+    if kind == "linear":
+        return base * (1.0 - frac)
+    return base * 0.5 * (1.0 + math.cos(math.pi * frac))
 
 
 def save_periodic_state(engine, output_dir: str, step: int, rank: int, world: int) -> None:
