@@ -141,6 +141,12 @@ class SlideFSDP(nn.Module):
         self.rank = dist.get_rank() if dist.is_initialized() else 0
         self.world_size = dist.get_world_size() if dist.is_initialized() else 1
         self.is_cuda = self.device.type == "cuda"
+        local_ranks = int(os.environ.get("LOCAL_WORLD_SIZE", str(self.world_size)) or self.world_size)
+        if self.world_size > 1 and local_ranks < self.world_size:
+            # the master weights and the update counters live in one node's
+            # shared host memory (as the reference's /dev/shm files do)
+            raise NotImplementedError(
+                f"SlideFSDP runs on one node: WORLD_SIZE={self.world_size} but LOCAL_WORLD_SIZE={local_ranks}")
         if self.is_cuda:
             torch.cuda.set_device(self.device)
         elif "OMP_NUM_THREADS" not in os.environ:

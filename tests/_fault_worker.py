@@ -70,3 +70,24 @@ def run_mismatch(rank, world, port, out_path):
         result["error"] = f"{type(exc).__name__}: {exc}"
     torch.save(result, out_path + f".{rank}")
     os._exit(0)
+
+
+def run_multinode(rank, world, port, out_path):
+    """Two ranks that claim to sit on different nodes (one local rank
+    each): both must refuse with a named error."""
+    from datetime import timedelta
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), LOCAL_RANK="0",
+                      LOCAL_WORLD_SIZE="1", T1_QUIET="1")
+    result = {"rank": rank, "error": None}
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+        from test1_b200 import SlideFSDPConfig
+        from test1_b200.models.llama import LlamaConfig, LlamaForCausalLM
+        from test1_b200.slide_fsdp import SlideFSDP
+
+        SlideFSDP(LlamaForCausalLM(LlamaConfig.tiny()), SlideFSDPConfig(dtype=torch.float32, device="cpu"))
+    except Exception as exc:
+        result["error"] = f"{type(exc).__name__}: {exc}"
+    torch.save(result, out_path + f".{rank}")
+    os._exit(0)

@@ -8,7 +8,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from tests._fault_worker import run, run_mismatch
+from tests._fault_worker import run, run_mismatch, run_multinode
 
 
 def _port():
@@ -95,3 +95,17 @@ def test_region_header_detects_overwrite_and_corruption(tmp_path):
         peer.close()
     finally:
         owner.close()
+
+
+def test_ranks_on_several_nodes_are_refused(tmp_path):
+    out = str(tmp_path / "res")
+    ctx = mp.get_context("spawn")
+    port = _port()
+    ps = [ctx.Process(target=run_multinode, args=(r, 2, port, out)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=120)
+    for r in range(2):
+        err = torch.load(out + f".{r}")["error"]
+        assert err is not None and "runs on one node" in err, err
