@@ -27,7 +27,7 @@ on data dependencies):
             the bf16 shadow that the next forward copies to the GPU.
 
 Compared with the reference: no autograd hooks or per-layer autograd
-Functions (so no hook-ordering races, survey of slide_fsdp.py:416-430), no
+Functions (so none of the hook-ordering races of slide_fsdp.py:416-430), no
 per-pass fp32->bf16 CPU cast (the optimizer writes the shadow), the embedding
 backward does not reload the embedding weights, and the optimizer is sharded
 across ranks.

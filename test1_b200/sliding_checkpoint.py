@@ -10,7 +10,7 @@ to the preallocated pinned slot ``layer_tensors[i-1][k]``; the last layer
 keeps its tensors on the GPU; on the first unpack of layer i the slots of
 layer i-1 are copied back to the GPU on a side stream.
 
-Differences (fixes of defects the survey lists):
+Differences from the reference (sliding_checkpoint.py:11-202), each fixing one of its defects:
   * the GPU tensor being offloaded is kept alive (``record_stream``) until
     its copy on the side stream completed;
   * prefetched buffers are keyed by layer, not a global FIFO, so an
