@@ -1,0 +1,78 @@
+"""Utilities without a GPU: the NVML sampler against a fake library,
+the module printer, the memory report, sharded HF checkpoint I/O."""
+import os
+import time
+import types
+
+import torch
+
+from test1_b200.utils import checkpoint_io
+from test1_b200.utils.gpu_monitor import GPUMonitor
+from test1_b200.utils.log_mem import log_memory_stats
+from test1_b200.utils.module_utils import module_tree
+
+
+class _FakeNVML:
+    NVML_CLOCK_SM = 1
+
+    def __init__(self):
+        self.calls = []
+
+    def nvmlInit(self):
+        self.calls.append("init")
+
+    def nvmlShutdown(self):
+        self.calls.append("shutdown")
+
+    def nvmlDeviceGetHandleByIndex(self, i):
+        return ("gpu", i)
+
+    def nvmlDeviceGetUtilizationRates(self, h):
+        return types.SimpleNamespace(gpu=90, memory=40)
+
+    def nvmlDeviceGetClockInfo(self, h, kind):
+        return 1965
+
+    def nvmlDeviceGetMemoryInfo(self, h):
+        return types.SimpleNamespace(used=12e9)
+
+    def nvmlDeviceGetCurrentClocksEventReasons(self, h):
+        return 0x4  # sw power cap
+
+    # any setter would be a bug: the monitor only reads
+    def __getattr__(self, name):
+        if name.startswith("nvmlDeviceSet") or name.startswith("nvmlDeviceReset"):
+            raise AssertionError(f"GPUMonitor called {name}")
+        raise AttributeError(name)
+
+
+def test_gpu_monitor_samples_and_only_reads():
+    nv = _FakeNVML()
+    mon = GPUMonitor(device_index=3, interval_s=0.005, nvml=nv).start()
+    time.sleep(0.1)
+    s = mon.stop()
+    assert nv.calls[0] == "init" and nv.calls[-1] == "shutdown"
+    assert s["samples"] >= 3 and s["gpu_util_mean"] == 90 and s["sm_mhz_median"] == 1965
+    assert abs(s["mem_used_gb_max"] - 12.0) < 1e-9
+    assert all(x["reasons"] == 4 for x in mon.samples)
+
+
+def test_module_tree_and_memory_report():
+    m = torch.nn.Sequential(torch.nn.Linear(4, 8), torch.nn.ReLU(), torch.nn.Linear(8, 2))
+    text = module_tree(m)
+    assert "Linear" in text and "58" in text  # 4*8+8 + 8*2+2 parameters
+    assert isinstance(log_memory_stats("x"), str)
+
+
+def test_sharded_hf_checkpoint_round_trip(tmp_path):
+    g = torch.Generator().manual_seed(0)
+    tensors = {f"layer.{i}.weight": torch.randn(64, 64, generator=g) for i in range(5)}
+    # shards of 2 tensors (64 * 64 * 2 bytes each in bf16)
+    checkpoint_io.save_hf_checkpoint(str(tmp_path), {"model_type": "llama"}, tensors, torch.bfloat16,
+                                     shard_bytes=2 * 64 * 64 * 2)
+    files = sorted(f for f in os.listdir(tmp_path) if f.endswith(".safetensors"))
+    assert len(files) == 3 and os.path.exists(tmp_path / "model.safetensors.index.json")
+    cfg, back = checkpoint_io.load_hf_checkpoint(str(tmp_path))
+    assert cfg["model_type"] == "llama"
+    for n, t in tensors.items():
+        assert torch.equal(back[n], t.bfloat16()), n
