@@ -143,3 +143,20 @@ def test_bench_presets_follow_host_ram():
     assert big["master_layout"] == "split" and big["state_dtype"] == "fp32"
     assert bench.baseline_preset(3, 0)["seq"] == 4096 and bench.baseline_preset(2, 0) == {}
     assert bench.host_ram_bytes() > 0
+
+
+def test_host_traffic_model():
+    import importlib.util
+    import os
+
+    spec = importlib.util.spec_from_file_location(
+        "htm", os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "benchmark",
+                            "host_traffic_model.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    assert m.bytes_per_param(1, "full") == 32.0
+    assert m.bytes_per_param(8, "full") == 26 + 32 + 2
+    assert m.bytes_per_param(8, "shard") == 32.0
+    rows = m.predict(8.03e9, 190.0, 4096, gpus=(1, 2))
+    assert [r["mode"] for r in rows] == ["full", "full", "shard"]
+    assert abs(rows[0]["step_s"] - 32 * 8.03e9 / 190e9) < 1e-3
