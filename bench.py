@@ -53,6 +53,9 @@ def parse_args():
                    help="comparison config preset: 2 = 8B full + gpu_reduce, batch 4 x 1024 (default); "
                         "3 = 8B shard + gpu_reduce, AC cpu, batch 2 x 4096; 4 = 70B shard + cpu_reduce, "
                         "batch 1 x 2048, bf16 weights and Adam state in host RAM (fp32 with >= 1.2 TB)")
+    p.add_argument("--no-fuse-gather-qkv", action="store_true",
+                   help="shard mode: prefetch each layer with the standalone fused gather instead of "
+                        "gathering it inside its QKV GEMM")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--profile-json", default="")
     args = p.parse_args()
@@ -192,7 +195,8 @@ def run_ours(args, rank, world, local):
                           grad_sync_mode=args.grad_sync_mode, gpu_buffer_pool_size=args.pool,
                           lr=1e-5, weight_decay=0.01, ac_offload_mode=args.ac_offload,
                           max_seq_length=args.seq, train_batch_size=args.batch, seed=42,
-                          master_layout=args.master_layout, optimizer_state_dtype=args.state_dtype)
+                          master_layout=args.master_layout, optimizer_state_dtype=args.state_dtype,
+                          fuse_gather_qkv=not args.no_fuse_gather_qkv)
     t0 = time.time()
     engine = SlideFSDP(model, cfg)
     init_s = time.time() - t0
@@ -332,6 +336,7 @@ def main():
             "parallelism": f"dp{world}",
             "param_transfer_mode": args.param_transfer_mode, "grad_sync_mode": args.grad_sync_mode,
             "gpu_buffer_pool_size": args.pool, "ac_offload_mode": args.ac_offload,
+            **({"fuse_gather_qkv": not args.no_fuse_gather_qkv} if args.param_transfer_mode == "shard" else {}),
             "l2": "no flush: ~30 GB of weights stream host->device per step (>> 126 MB L2)",
         },
         "clocks": res.get("clocks"),

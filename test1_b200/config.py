@@ -42,6 +42,11 @@ Extra fields (all optional, reference configs never set them):
         there are several.
     use_native_kernels: run the model on the sm_100a kernels (True) or on
         plain PyTorch ops (False; the CPU test path).
+    fuse_gather_qkv: in shard mode the forward gathers each decoder layer
+        inside its QKV GEMM kernel (True, default).  False gathers it with
+        the standalone fused gather on the copy stream one layer ahead (as
+        the backward always does), taking the gather off the forward's
+        critical path at the cost of the fusion.
 """
 from __future__ import annotations
 
@@ -108,6 +113,7 @@ class SlideFSDPConfig:
     master_layout: str = "split"  # "split" (hi/lo 16-bit planes), "fp32" (fp32 + bf16 shadow) or "bf16"
     optimizer_state_dtype: str = "fp32"  # LayerAdam m/v in host memory: "fp32" or "bf16"
     use_native_kernels: Optional[bool] = None  # None: native iff device is CUDA
+    fuse_gather_qkv: bool = True  # shard mode: gather each layer inside its QKV GEMM
     trace_path: Optional[str] = None  # per-phase step trace (JSON lines); env T1_TRACE also enables it
 
     def __post_init__(self):

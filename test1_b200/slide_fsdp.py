@@ -828,7 +828,8 @@ class SlideFSDP(nn.Module):
         # ---------------- forward
         self._fetch(emb, with_grad=False)
         fuse_first = (L > 0 and not self.generic and hasattr(self.comm, "can_fuse_qkv")
-                      and self.comm.can_fuse_qkv(S[1]) and self.config.use_native_kernels)
+                      and self.comm.can_fuse_qkv(S[1]) and self.config.use_native_kernels
+                      and self.config.fuse_gather_qkv)
         if L > 0 and not fuse_first:
             self._fetch(S[1], with_grad=False)
         self._wait_loaded(emb)
