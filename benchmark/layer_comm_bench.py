@@ -10,6 +10,8 @@ Llama-3.1-8B decoder layer (218,112,000 params, bf16 on the GPU), 2..8 GPUs:
       shard                                  -- fused_rs_d2h
       vs. NCCL path: reduce_scatter_tensor + scale + D2H copy
   (c) LayerAdam host step on this rank's shard of the layer
+  (d) the same operations through the reference's own DistributedSync,
+      unmodified (shard all-gather + cuBLAS QKV; reduce to rank 0 + D2H)
 
 Roofline per fused path = the slowest of: FLOPs / measured bf16 peak, bytes
 crossing PCIe / 55 GB/s (measured per-direction host link on this pool), bytes
@@ -63,6 +65,24 @@ def maxr(x):
     t = torch.tensor([x], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def _reference_sync(dev):
+    """The reference's DistributedSync for shard + gpu_reduce, or None when
+    its source is not installed under baseline/_ref."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "distributed_sync.py")):
+        return None
+    import types
+
+    sys.path.insert(0, ref_dir)
+    try:
+        from distributed_sync import DistributedSync  # the reference's module
+    finally:
+        sys.path.remove(ref_dir)
+    cfg = types.SimpleNamespace(param_transfer_mode="shard", grad_sync_mode="gpu_reduce", device=dev,
+                                dtype=torch.bfloat16)
+    return DistributedSync(cfg)
 
 
 def main():
@@ -136,6 +156,32 @@ def main():
     tnb = maxr(timed(nccl_b))
     code = int(err.item())
 
+    # (d) the reference's own path on the same layer (its DistributedSync,
+    # distributed_sync.py:99-158 and :242-300, run unmodified): H2D of this
+    # rank's slice of its pinned bf16 staging copy, a host synchronisation,
+    # all_gather into fresh tensors and copies into the unit, then the QKV
+    # GEMM by cuBLAS; gradients reduced to rank 0 in full, averaged and copied
+    # to host there.  Its per-pass CPU fp32->bf16 cast into the staging copy
+    # (layer_state.py:301) is not timed.
+    td_a = td_b = None
+    ref_sync = _reference_sync(dev) if world > 1 else None
+    if ref_sync is not None:
+        staging = torch.empty(P, dtype=torch.bfloat16, pin_memory=True)
+        staging.copy_(torch.randn(P) * 0.02)
+        ref_unit = torch.empty(P, dtype=torch.bfloat16, device=dev)
+        ref_grads = torch.randn(P, device=dev).bfloat16()
+        ref_host = torch.empty(P, dtype=torch.bfloat16, pin_memory=True)
+
+        def ref_a():
+            ref_sync.gather_params_to_gpu(staging, ref_unit, None)
+            torch.matmul(x, ref_unit[: n_qkv * H].view(n_qkv, H).t(), out=qkv)
+
+        def ref_b():
+            ref_sync.reduce_gradients_to_master(ref_grads, ref_host, None)
+
+        td_a = maxr(timed(ref_a))
+        td_b = maxr(timed(ref_b))
+
     # (c) host LayerAdam on this rank's shard (split master, bf16 grad)
     m = torch.zeros(n)
     v = torch.zeros(n)
@@ -160,6 +206,8 @@ def main():
             "b_fused_rs_d2h_ms": round(tb, 3), "b_nccl_reduce_scatter_d2h_ms": round(tnb, 3),
             "b_roofline_ms": round(roof_b, 3), "b_frac_of_roofline": round(roof_b / tb, 3),
             "c_layeradam_shard_ms": round(tc, 2),
+            "d_reference_shard_gather_qkv_ms": None if td_a is None else round(td_a, 3),
+            "d_reference_reduce_to_rank0_d2h_ms": None if td_b is None else round(td_b, 3),
             "roofline_inputs": {"pcie_gbs": PCIE_GBS, "nvlink_gbs": NVLINK_GBS, "bf16_tflops": peak,
                                 "peak_ref": tag},
         }
