@@ -125,6 +125,17 @@ def test_state_saved_at_one_world_size_resumes_at_another(tmp_path, world_a, wor
         mb, vb, sb = _full_optimizer_state(b, i, world_b)
         assert torch.equal(ma, mb) and torch.equal(va, vb), i
         assert sa == sb == {2}, (sa, sb)
+    if world_b == 1:
+        # a missing shard file is reported, not silently zero-filled
+        os.remove(os.path.join(a, "optim_rank1_layer_1.pt"))
+        torch.manual_seed(0)
+        eng = SlideFSDP(LlamaForCausalLM(LlamaConfig.tiny()),
+                        SlideFSDPConfig(dtype=torch.float32, device="cpu", lr=1e-3))
+        try:
+            with pytest.raises(ValueError, match="layer 1: the saved optimizer shards cover"):
+                eng.load_state(a)
+        finally:
+            eng.close()
 
 
 def test_train_cli_periodic_state_and_resume(tmp_path):
