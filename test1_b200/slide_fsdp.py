@@ -171,6 +171,11 @@ class SlideFSDP(nn.Module):
                 self.generic = True
         if getattr(model.config, "tie_word_embeddings", False):
             raise NotImplementedError("tied input/output embeddings are not supported by layer sliding")
+        if not self.generic and config.use_native_kernels and self.dtype != torch.bfloat16:
+            # fail here rather than at the first kernel of the first step
+            raise NotImplementedError(
+                f"the sm_100a Llama kernels compute in bfloat16; dtype={self.dtype} runs on the "
+                f"generic layer path (other HF architectures) or with use_native_kernels=False")
         self.base_model = model
         self.model_config = model.config
         self._split_model(model)

@@ -206,3 +206,9 @@ def test_per_step_learning_rate_schedule_matches_adamw():
             assert d.max().item() < 4 * 5e-3, n
     finally:
         eng.close()
+
+
+def test_fp16_on_the_native_llama_kernels_is_refused_early():
+    cfg = SlideFSDPConfig(dtype=torch.float16, device="cpu", use_native_kernels=True)
+    with pytest.raises(NotImplementedError, match="compute in bfloat16"):
+        SlideFSDP(LlamaForCausalLM(LlamaConfig.tiny()), cfg)
