@@ -9,20 +9,26 @@ import torch
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from test1_b200.ops import native  # noqa: E402
 
-kind = sys.argv[1] if len(sys.argv) > 1 else "fwd"
-if "--pair" in sys.argv:
-    native.gemm_set_mode(1)
-M, N, K = 4096, 6144, 4096
-x = torch.randn(M, K, device="cuda").bfloat16()
-w = torch.randn(N, K, device="cuda").bfloat16()
-dy = torch.randn(M, N, device="cuda").bfloat16()
-for _ in range(3):
-    if kind == "fwd":
-        native.gemm(x, w, torch.empty(M, N, device="cuda", dtype=torch.bfloat16))
-    elif kind == "dgrad":
-        native.gemm(dy, w, torch.empty(M, K, device="cuda", dtype=torch.bfloat16), False, True)
-    else:
-        native.gemm(dy, x, torch.empty(N, K, device="cuda", dtype=torch.bfloat16), True, True)
-torch.cuda.synchronize()
-assert native.gemm_error() == 0
-print("ok", kind)
+
+def main() -> None:
+    kind = sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else "fwd"
+    if "--pair" in sys.argv:
+        native.gemm_set_mode(1)
+    M, N, K = 4096, 6144, 4096
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    w = torch.randn(N, K, device="cuda").bfloat16()
+    dy = torch.randn(M, N, device="cuda").bfloat16()
+    for _ in range(3):
+        if kind == "fwd":
+            native.gemm(x, w, torch.empty(M, N, device="cuda", dtype=torch.bfloat16))
+        elif kind == "dgrad":
+            native.gemm(dy, w, torch.empty(M, K, device="cuda", dtype=torch.bfloat16), False, True)
+        else:
+            native.gemm(dy, x, torch.empty(N, K, device="cuda", dtype=torch.bfloat16), True, True)
+    torch.cuda.synchronize()
+    assert native.gemm_error() == 0
+    print("ok", kind)
+
+
+if __name__ == "__main__":
+    main()
