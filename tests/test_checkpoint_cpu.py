@@ -183,3 +183,18 @@ def test_train_cli_learning_rate_schedule(tmp_path):
     lrs = [float(x) for x in re.findall(r"\| lr ([0-9.e+-]+)", r.stdout)]
     want = [tm.scheduled_lr(1e-3, s, 4, 2, "cosine") for s in range(4)]
     assert len(lrs) == 4 and all(math.isclose(a, b, rel_tol=1e-2) for a, b in zip(lrs, want)), (lrs, want)
+
+
+def test_train_cli_pins_the_main_thread_to_control_cores(tmp_path):
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cpu = sorted(os.sched_getaffinity(0))[0]
+    code = ("import os, sys; sys.argv = ['train.py']; sys.path.insert(0, %r); import train; "
+            "train.pin_main_thread(0); print(sorted(os.sched_getaffinity(0)))" % root)
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300, cwd=root,
+                       env=dict(os.environ, NUMA_CONTROL_CORES=str(cpu)))
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert r.stdout.strip().endswith(f"[{cpu}]")

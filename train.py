@@ -85,7 +85,30 @@ def init_distributed(device_type: str):
     if world > 1 and not dist.is_initialized():
         dist.init_process_group("nccl" if device_type == "cuda" else "gloo",
                                 timeout=timedelta(seconds=900))
+    pin_main_thread(rank)
     return rank, world, local
+
+
+def pin_main_thread(rank: int) -> None:
+    """Pin the launching thread to the control cores numa_launch.sh chose
+    (NUMA_CONTROL_CORES, a CPU list such as "0-1,8"), as the reference's
+    train.py does; the host worker pool pins its own threads to
+    NUMA_CPU_ADAM_CORES."""
+    spec = os.environ.get("NUMA_CONTROL_CORES", "").strip()
+    if not spec:
+        return
+    cpus = []
+    for part in spec.split(","):
+        part = part.strip()
+        if "-" in part:
+            a, b = part.split("-", 1)
+            cpus.extend(range(int(a), int(b) + 1))
+        elif part:
+            cpus.append(int(part))
+    try:
+        os.sched_setaffinity(0, cpus)
+    except OSError as exc:
+        print(f"[rank {rank}] could not pin the main thread to {spec}: {exc}", flush=True)
 
 
 def build_model(args, config):
