@@ -312,6 +312,22 @@ def main():
     else:
         res = run_ours(args, rank, world, local)
 
+    line = make_line(args, world, res)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+        if args.profile_json:
+            with open(args.profile_json, "w") as f:
+                json.dump(line, f, indent=2)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def make_line(args, world: int, res: dict) -> dict:
+    """The one JSON line of a run: ``res`` holds the device-timed
+    milliseconds of the timed steps (max over ranks) and the run's details."""
     tokens = args.batch * args.seq * world * args.steps
     value = tokens / (res["dev_ms"] / 1e3)
     line = {
@@ -351,16 +367,7 @@ def main():
                                  "fetch_blocked_on_adam_s_per_step", "comm", "losses",
                                  "attn_implementation") if k in res}
     line["detail"] = extra
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-        if args.profile_json:
-            with open(args.profile_json, "w") as f:
-                json.dump(line, f, indent=2)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-        dist.destroy_process_group()
+    return line
 
 
 if __name__ == "__main__":

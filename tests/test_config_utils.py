@@ -160,3 +160,33 @@ def test_host_traffic_model():
     rows = m.predict(8.03e9, 190.0, 4096, gpus=(1, 2))
     assert [r["mode"] for r in rows] == ["full", "full", "shard"]
     assert abs(rows[0]["step_s"] - 32 * 8.03e9 / 190e9) < 1e-3
+
+
+def test_bench_line_carries_the_contract_fields():
+    import importlib.util
+    import os
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_line", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    argv, sys.argv = sys.argv, ["bench.py", "--steps", "4", "--warmup", "3"]
+    try:
+        args = bench.parse_args()
+    finally:
+        sys.argv = argv
+    res = {"dev_ms": 4 * 1480.0, "clocks": {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []},
+           "e2e": {"value": 2700.0, "unit": "tokens/s", "h2d_bytes_per_step": 32768, "d2h_bytes_per_step": 4},
+           "launches": 4600, "init_s": 12.0}
+    line = bench.make_line(args, 8, res)
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+              "scaling", "vs_baseline", "dtype", "data", "config", "clocks", "e2e", "gpu_launches"):
+        assert k in line, k
+    assert line["metric"] == bench.METRIC and line["n_gpus"] == 8 and line["scaling"] == "weak"
+    assert abs(line["value"] - 8 * 4 * 1024 * 4 / (4 * 1.48)) < 0.01  # whole-job tokens/s
+    assert line["ms_per_step"] == 1480.0 and line["higher_is_better"] is True
+    for k in ("model", "global_batch", "seq_len", "parallelism"):
+        assert k in line["config"], k
+    assert line["config"]["global_batch"] == 32 and line["config"]["parallelism"] == "dp8"
+    assert line["gpu_launches"] == 4600 and line["detail"]["init_s"] == 12.0
