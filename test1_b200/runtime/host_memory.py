@@ -181,6 +181,14 @@ class HostRegion:
             raise ValueError("misaligned view")
         return self.buf[offset_bytes:end].view(dtype)
 
+    def unlink(self) -> None:
+        """Remove the shared-memory file while the mappings stay valid: once
+        every process that needs the region has mapped it, nothing can leak
+        it any more, not even a process that dies without cleaning up."""
+        if self.shm_path is not None and self.owner:
+            _native.host().shm_remove(self.shm_path)
+            self.owner = False
+
     def close(self) -> None:
         if getattr(self, "buf", None) is None:
             return

@@ -240,6 +240,10 @@ class SlideFSDP(nn.Module):
             dist.barrier()
         if not creator:
             check_region_header(self.shared, self._hdr_off, header, self.rank)
+        if self.world_size > 1:
+            dist.barrier()  # every local rank has mapped the region
+            if creator:
+                self.shared.unlink()
         self.counters = self.shared.view(torch.uint8, self._ctr_off, 8 * n_counters)
         phase("shared_region")
 
