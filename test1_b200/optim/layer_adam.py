@@ -30,13 +30,14 @@ from typing import Any, DefaultDict, Dict, Iterable, Optional
 import torch
 
 from .. import _native
+from ..runtime.scratch_file import ScratchFile
 
 
 class _StateOffloader:
     """Moves per-layer state tensors to files and back.
 
-    ``offload(key, t)`` writes ``t`` to ``<dir>/offload-<pid>-<key>.bin`` on a
-    background thread and drops the in-memory tensor once written;
+    ``offload(key, t)`` writes ``t`` to the key's nameless scratch file in
+    ``<dir>`` (runtime/scratch_file.py) on a background thread and drops the in-memory tensor once written;
     ``prefetch(key)`` reads it back into a fresh tensor on the same thread
     pool; ``get(key)`` waits for the pending operation and returns the
     resident tensor.  Operations on one key are ordered (each waits for the
@@ -50,9 +51,13 @@ class _StateOffloader:
         self.pending: Dict[Any, Any] = {}
         self.meta: Dict[Any, tuple] = {}
         self.tensors: Dict[Any, Optional[torch.Tensor]] = {}
+        self.files: Dict[Any, ScratchFile] = {}  # nameless: nothing outlives the process
 
-    def _path(self, key) -> str:
-        return os.path.join(self.dir, f"offload-{os.getpid()}-{key[0]}-{key[1]}.bin")
+    def _file(self, key) -> ScratchFile:
+        f = self.files.get(key)
+        if f is None:
+            f = self.files[key] = ScratchFile(self.dir)
+        return f
 
     def _wait(self, key) -> None:
         f = self.pending.pop(key, None)
@@ -64,10 +69,11 @@ class _StateOffloader:
         self.meta[key] = (t.numel(), t.dtype)
         self.tensors[key] = t
 
+        file = self._file(key)
+
         def job():
             raw = t.view(torch.uint8) if t.dtype != torch.uint8 else t
-            with open(self._path(key), "wb") as fh:
-                fh.write(memoryview(raw.numpy()))
+            file.write(memoryview(raw.numpy()))
             self.tensors[key] = None
 
         self.pending[key] = self.pool.submit(job)
@@ -80,9 +86,7 @@ class _StateOffloader:
         def job():
             numel, dtype = self.meta[key]
             t = torch.empty(numel, dtype=dtype)
-            raw = t.view(torch.uint8)
-            with open(self._path(key), "rb") as fh:
-                fh.readinto(memoryview(raw.numpy()))
+            self.files[key].read_into(memoryview(t.view(torch.uint8).numpy()))
             self.tensors[key] = t
 
         self.pending[key] = self.pool.submit(job)
@@ -98,12 +102,9 @@ class _StateOffloader:
 
     def close(self):
         self.pool.shutdown(wait=True)
-        for name in os.listdir(self.dir):
-            if name.startswith(f"offload-{os.getpid()}-"):
-                try:
-                    os.remove(os.path.join(self.dir, name))
-                except OSError:
-                    pass
+        for f in self.files.values():
+            f.close()
+        self.files.clear()
 
 
 class LayerAdam:

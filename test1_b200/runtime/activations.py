@@ -13,7 +13,8 @@ sliding_checkpoint.py:51-131).  Modes:
         while layer i runs (one layer ahead)
   nvme  hold no per-layer host copy: the side-stream copy lands in one of a
         small ring of page-locked staging buffers, an I/O thread writes it to
-        a file under ``ac_offload_dir`` and frees the buffer; in the
+        a nameless file in ``ac_offload_dir`` (runtime/scratch_file.py: no
+        file outlives the process) and frees the buffer; in the
         backward the I/O thread reads the file one layer ahead into a staging
         buffer and issues the host-to-device copy itself, so neither the
         read nor the copy sits on the compute path.  (The reference's
@@ -36,6 +37,7 @@ from typing import Dict, Optional
 import torch
 
 from .device import Event, Stream
+from .scratch_file import ScratchFile
 
 
 class _StagingRing:
@@ -84,6 +86,7 @@ class ActivationStore:
         self._write_futs: Dict[int, Future] = {}
         self._read_futs: Dict[int, Future] = {}
         self._meta: Dict[int, tuple] = {}
+        self._files: Dict[int, ScratchFile] = {}  # nvme: one nameless file per layer
         self._ring = _StagingRing(staging_buffers, self.cuda) if mode == "nvme" else None
         self._io = ThreadPoolExecutor(max_workers=2, thread_name_prefix="t1-acio") if mode == "nvme" else None
         if mode == "nvme":
@@ -100,8 +103,11 @@ class ActivationStore:
             self._host[i] = t
         return t
 
-    def _path(self, i: int) -> str:
-        return os.path.join(self.dir, f"act-{os.getpid()}-{id(self)}-{i}.bin")
+    def _file(self, i: int) -> ScratchFile:
+        f = self._files.get(i)
+        if f is None:
+            f = self._files[i] = ScratchFile(self.dir)
+        return f
 
     def _d2h_copy(self, dst: torch.Tensor, h: torch.Tensor) -> Event:
         ready = Event(self.device).record()  # h produced on the current stream
@@ -131,11 +137,12 @@ class ActivationStore:
         if prev is not None:
             prev.result()
 
-        def write(i=i, buf=buf, ev=ev, nbytes=nbytes):
+        file = self._file(i)
+
+        def write(buf=buf, ev=ev, nbytes=nbytes, file=file):
             try:
                 ev.synchronize()
-                with open(self._path(i), "wb") as f:
-                    f.write(memoryview(buf[:nbytes].numpy()))
+                file.write(memoryview(buf[:nbytes].numpy()))
             finally:
                 self._ring.release(buf)
 
@@ -174,8 +181,7 @@ class ActivationStore:
                 wfut.result()
             buf = self._ring.acquire(nbytes)
             try:
-                with open(self._path(i), "rb") as f:
-                    f.readinto(memoryview(buf[:nbytes].numpy()))
+                self._files[i].read_into(memoryview(buf[:nbytes].numpy()))
                 src = buf[:nbytes].view(out.dtype).view(out.shape)
                 if self.cuda:
                     with torch.cuda.device(self.device):
@@ -224,10 +230,8 @@ class ActivationStore:
                 except Exception:
                     pass
             self._io.shutdown(wait=True)
-            for i in list(self._meta):
-                try:
-                    os.remove(self._path(i))
-                except OSError:
-                    pass
+        for f in self._files.values():
+            f.close()
+        self._files.clear()
         self._host.clear()
         self._gpu.clear()

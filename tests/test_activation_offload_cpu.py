@@ -40,6 +40,6 @@ def test_offload_modes_match_gpu_mode(mode, tmp_path):
     assert stats["ac_d2h_bytes"] > 0 and stats["ac_h2d_bytes"] == stats["ac_d2h_bytes"]
     if mode == "nvme":
         assert host_slots == 0  # nothing kept per layer in host memory
-        assert not os.listdir(tmp_path / "acts")  # files removed at close
+        assert not os.listdir(tmp_path / "acts")  # the offload files have no names
     else:
         assert host_slots == L - 1  # the last layer's input stays on the device

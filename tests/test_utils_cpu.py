@@ -76,3 +76,19 @@ def test_sharded_hf_checkpoint_round_trip(tmp_path):
     assert cfg["model_type"] == "llama"
     for n, t in tensors.items():
         assert torch.equal(back[n], t.bfloat16()), n
+
+
+def test_scratch_files_have_no_name_and_round_trip(tmp_path):
+    from test1_b200.runtime.scratch_file import ScratchFile
+
+    f = ScratchFile(str(tmp_path))
+    data = torch.arange(1 << 20, dtype=torch.int32)
+    f.write(memoryview(data.numpy()))
+    out = torch.empty_like(data)
+    f.read_into(memoryview(out.numpy()))
+    assert torch.equal(out, data)
+    f.write(memoryview(data[:10].neg().numpy()), offset=8)  # positional, partial overwrite
+    f.read_into(memoryview(out.numpy()))
+    assert torch.equal(out[2:12], data[:10].neg()) and torch.equal(out[12:], data[12:])
+    assert os.listdir(tmp_path) == []  # nothing to leak
+    f.close()
