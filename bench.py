@@ -142,6 +142,24 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.rows)}
 
 
+def merge_clocks(local: dict, world: int) -> dict:
+    """Every rank sampled its own GPU; the line reports the slowest GPU's
+    median SM clock, the union of throttle reasons over all GPUs, and each
+    GPU's own record (a collective: every rank calls it once)."""
+    if world == 1 or local is None:
+        return local
+    import torch.distributed as dist
+
+    recs = [None] * world
+    dist.all_gather_object(recs, local)
+    meds = [r.get("sm_mhz") for r in recs if r and r.get("sm_mhz") is not None]
+    maxes = [r.get("sm_max_mhz") for r in recs if r and r.get("sm_max_mhz") is not None]
+    reasons = sorted({x for r in recs if r for x in r.get("reasons", [])})
+    return {"sm_mhz": min(meds) if meds else None, "sm_max_mhz": max(maxes) if maxes else None,
+            "reasons": reasons, "samples": sum((r or {}).get("samples", 0) for r in recs),
+            "per_gpu": recs}
+
+
 def init_dist(args):
     import torch
     import torch.distributed as dist
@@ -312,6 +330,7 @@ def main():
     else:
         res = run_ours(args, rank, world, local)
 
+    res["clocks"] = merge_clocks(res.get("clocks"), world)
     line = make_line(args, world, res)
     if rank == 0:
         print(json.dumps(line), flush=True)

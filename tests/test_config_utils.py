@@ -190,3 +190,26 @@ def test_bench_line_carries_the_contract_fields():
         assert k in line["config"], k
     assert line["config"]["global_batch"] == 32 and line["config"]["parallelism"] == "dp8"
     assert line["gpu_launches"] == 4600 and line["detail"]["init_s"] == 12.0
+
+
+def test_bench_clock_records_merge_over_gpus(monkeypatch):
+    import importlib.util
+    import os
+
+    import torch.distributed as dist
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_clk", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    recs = [{"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": [], "samples": 10},
+            {"sm_mhz": 1800.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 9}]
+
+    def fake_gather(out, obj):
+        out[:] = recs
+
+    monkeypatch.setattr(dist, "all_gather_object", fake_gather)
+    m = bench.merge_clocks(recs[0], 2)
+    assert m["sm_mhz"] == 1800.0 and m["reasons"] == ["sw_power_cap"] and m["samples"] == 19
+    assert m["per_gpu"] == recs
+    assert bench.merge_clocks(recs[0], 1) is recs[0]
