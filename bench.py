@@ -93,22 +93,50 @@ def baseline_preset(cfg: int, ram_bytes: int) -> dict:
 
 
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons while running."""
+    """Samples nvidia-smi SM clocks and throttle reasons of this rank's GPU
+    while running.  The GPU is found by its PCI bus id (CUDA's device index
+    and nvidia-smi's differ when only some of the node's GPUs are visible),
+    falling back to the index."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,pci.bus_id")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
+        self.bus = self._bus_id(gpu_index)
         self.rows = []
         self.proc = None
+
+    @staticmethod
+    def _bus_id(idx: int):
+        try:
+            import torch
+
+            p = torch.cuda.get_device_properties(idx)
+            return (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+        except Exception:
+            return None
+
+    def _on_bus(self, parts) -> bool:
+        if self.bus is None:
+            return False
+        try:
+            dom, rest = parts[9].split(":", 1)
+            bus, dev = rest.split(":", 1)
+            return (int(dom, 16), int(bus, 16), int(dev.split(".")[0], 16)) == self.bus
+        except (ValueError, IndexError):
+            return False
+
+    def _select(self, rows):
+        """This GPU's rows: matched by bus id, else by index."""
+        mine = [r for r in rows if self._on_bus(r)]
+        return mine or [r for r in rows if r[0] == str(self.gpu)]
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -118,7 +146,7 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
+            if len(parts) >= 10:
                 self.rows.append(parts)
 
     def stop(self) -> dict:
@@ -129,6 +157,7 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
+        self.rows = self._select(self.rows)
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]

@@ -213,3 +213,23 @@ def test_bench_clock_records_merge_over_gpus(monkeypatch):
     assert m["sm_mhz"] == 1800.0 and m["reasons"] == ["sw_power_cap"] and m["samples"] == 19
     assert m["per_gpu"] == recs
     assert bench.merge_clocks(recs[0], 1) is recs[0]
+
+
+def test_clock_sampler_picks_its_gpu_by_bus_id():
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_cs", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    cs = bench.ClockSampler.__new__(bench.ClockSampler)
+    cs.gpu, cs.bus = 0, (0, 0x1B, 0)
+    row = lambda idx, bus: [idx, "1965", "1965", "700", "0x0", "Not Active", "Not Active", "Not Active",
+                            "Active", bus]
+    rows = [row("0", "00000000:18:00.0"), row("3", "00000000:1B:00.0")]
+    assert cs._select(rows) == [rows[1]]  # CUDA device 0 is nvidia-smi GPU 3
+    cs.bus = (0, 0x99, 0)  # no bus matches: fall back to the index
+    assert cs._select(rows) == [rows[0]]
+    cs.bus = None
+    assert cs._select(rows) == [rows[0]]
