@@ -94,17 +94,16 @@ def baseline_preset(cfg: int, ram_bytes: int) -> dict:
 
 class ClockSampler:
     """Samples nvidia-smi SM clocks and throttle reasons of this rank's GPU
-    while running.  The GPU is found by its PCI bus id (CUDA's device index
-    and nvidia-smi's differ when only some of the node's GPUs are visible),
-    falling back to the index."""
+    while running.  nvidia-smi's index of the GPU is looked up by PCI bus id
+    (CUDA's device index differs from it when only some of the node's GPUs
+    are visible); if that lookup fails, the CUDA index is used."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap,pci.bus_id")
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.bus = self._bus_id(gpu_index)
+        self.gpu = self.smi_index(gpu_index, self._bus_id(gpu_index), self._smi_bus_table())
         self.rows = []
         self.proc = None
 
@@ -118,25 +117,35 @@ class ClockSampler:
         except Exception:
             return None
 
-    def _on_bus(self, parts) -> bool:
-        if self.bus is None:
-            return False
+    @staticmethod
+    def _smi_bus_table() -> str:
         try:
-            dom, rest = parts[9].split(":", 1)
-            bus, dev = rest.split(":", 1)
-            return (int(dom, 16), int(bus, 16), int(dev.split(".")[0], 16)) == self.bus
-        except (ValueError, IndexError):
-            return False
+            return subprocess.run(["nvidia-smi", "--query-gpu=index,pci.bus_id", "--format=csv,noheader"],
+                                  capture_output=True, text=True, timeout=20).stdout
+        except Exception:
+            return ""
 
-    def _select(self, rows):
-        """This GPU's rows: matched by bus id, else by index."""
-        mine = [r for r in rows if self._on_bus(r)]
-        return mine or [r for r in rows if r[0] == str(self.gpu)]
+    @staticmethod
+    def smi_index(cuda_index: int, bus, table: str) -> int:
+        """nvidia-smi index of the GPU on PCI address ``bus`` (domain, bus,
+        device) in ``table`` ("index, bus id" lines), else ``cuda_index``."""
+        if bus is not None:
+            for line in table.splitlines():
+                try:
+                    idx, bid = (x.strip() for x in line.split(",", 1))
+                    dom, rest = bid.split(":", 1)
+                    b, dev = rest.split(":", 1)
+                    if (int(dom, 16), int(b, 16), int(dev.split(".")[0], 16)) == tuple(bus):
+                        return int(idx)
+                except ValueError:
+                    continue
+        return cuda_index
 
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -146,7 +155,7 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 10:
+            if len(parts) >= 9:
                 self.rows.append(parts)
 
     def stop(self) -> dict:
@@ -157,7 +166,6 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        self.rows = self._select(self.rows)
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]

@@ -223,13 +223,8 @@ def test_clock_sampler_picks_its_gpu_by_bus_id():
     spec = importlib.util.spec_from_file_location("bench_cs", os.path.join(root, "bench.py"))
     bench = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(bench)
-    cs = bench.ClockSampler.__new__(bench.ClockSampler)
-    cs.gpu, cs.bus = 0, (0, 0x1B, 0)
-    row = lambda idx, bus: [idx, "1965", "1965", "700", "0x0", "Not Active", "Not Active", "Not Active",
-                            "Active", bus]
-    rows = [row("0", "00000000:18:00.0"), row("3", "00000000:1B:00.0")]
-    assert cs._select(rows) == [rows[1]]  # CUDA device 0 is nvidia-smi GPU 3
-    cs.bus = (0, 0x99, 0)  # no bus matches: fall back to the index
-    assert cs._select(rows) == [rows[0]]
-    cs.bus = None
-    assert cs._select(rows) == [rows[0]]
+    table = "0, 00000000:18:00.0\n3, 00000000:1B:00.0\n"
+    pick = bench.ClockSampler.smi_index
+    assert pick(0, (0, 0x1B, 0), table) == 3  # CUDA device 0 is nvidia-smi GPU 3
+    assert pick(1, (0, 0x99, 0), table) == 1  # unknown bus: the CUDA index
+    assert pick(2, None, table) == 2 and pick(2, (0, 0x18, 0), "") == 2
