@@ -39,6 +39,8 @@ def run_engine(rank, world, port, mode, grad, sharding, steps, out_path, ckpt, e
                                optimizer_sharding=sharding, enable_activation_checkpoint=ckpt,
                                **(extra or {}))
         eng = SlideFSDP(model, conf)
+        # the shared-memory file is gone once every rank has mapped it
+        assert eng.shared.shm_path is None or not os.path.exists(eng.shared.shm_path)
         losses = []
         for step_batches in batches(cfg, world, steps):
             ids = step_batches[rank]
