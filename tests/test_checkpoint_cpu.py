@@ -198,3 +198,17 @@ def test_train_cli_pins_the_main_thread_to_control_cores(tmp_path):
                        env=dict(os.environ, NUMA_CONTROL_CORES=str(cpu)))
     assert r.returncode == 0, r.stderr[-2000:]
     assert r.stdout.strip().endswith(f"[{cpu}]")
+
+
+def test_train_cli_memory_plan():
+    import json
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(root, "train.py"), "--model-config", "llama31_8b",
+                        "--device", "cpu", "--plan"], capture_output=True, text=True, timeout=300, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    plan = json.loads(r.stdout.strip().splitlines()[-1])
+    assert abs(plan["params"] - 8.03e9) < 0.01e9 and plan["host_total_gb"] > 100

@@ -92,3 +92,24 @@ def test_scratch_files_have_no_name_and_round_trip(tmp_path):
     assert torch.equal(out[2:12], data[:10].neg()) and torch.equal(out[12:], data[12:])
     assert os.listdir(tmp_path) == []  # nothing to leak
     f.close()
+
+
+def test_memory_plan_matches_the_engine_and_the_8b_layout():
+    from test1_b200 import SlideFSDPConfig
+    from test1_b200.models.llama import LlamaConfig, LlamaForCausalLM
+    from test1_b200.slide_fsdp import SlideFSDP
+    from test1_b200.utils.memory_plan import plan_memory
+
+    cfg = LlamaConfig.tiny()
+    conf = SlideFSDPConfig(dtype=torch.float32, device="cpu")
+    eng = SlideFSDP(LlamaForCausalLM(cfg), conf)
+    try:
+        p = plan_memory(cfg, conf, world=1, batch=2, seq=32)
+        assert p["params"] == eng.total_params
+        pool_elems = conf.gpu_buffer_pool_size * eng.pool.capacity + eng.big_pool.capacity
+        assert abs(p["device_pool_gb_per_gpu"] * 1e9 - pool_elems * 2 * 4) < 1
+    finally:
+        eng.close()
+    big = plan_memory(LlamaConfig.llama31_8b(), SlideFSDPConfig(dtype=torch.bfloat16, device="cpu"), world=1)
+    assert abs(big["host_master_gb"] - 32.12) < 0.01 and abs(big["host_optimizer_gb"] - 64.24) < 0.01
+    assert abs(big["host_grads_gb"] - 16.06) < 0.01

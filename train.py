@@ -42,6 +42,8 @@ def parse_args(argv=None):
     p.add_argument("--output-dir", type=str, default="./output")
     p.add_argument("--save-model", action="store_true")
     p.add_argument("--save-state", action="store_true", help="also save master + optimizer state")
+    p.add_argument("--plan", action="store_true",
+                   help="print the host and device memory this run needs (GB) and exit")
     p.add_argument("--lr-scheduler", choices=["constant", "linear", "cosine"], default="constant",
                    help="per-step learning-rate schedule after --warmup-steps of linear warm-up")
     p.add_argument("--warmup-steps", type=int, default=0)
@@ -156,6 +158,15 @@ def main(argv=None):
 
     model = build_model(args, config)
     mcfg = model.config
+    if args.plan:
+        from test1_b200.utils.memory_plan import plan_memory
+
+        if not hasattr(mcfg, "decoder_layer_params"):
+            raise SystemExit("--plan needs a Llama-structured model")
+        if rank == 0:
+            plan = plan_memory(mcfg, config, world, config.train_batch_size, config.max_seq_length)
+            print(json.dumps({k: round(v, 3) for k, v in plan.items()}), flush=True)
+        return
     flops = calculate_flops_per_batch(mcfg, config.train_batch_size, config.max_seq_length) * world
     engine = SlideFSDP(model, config)
     if args.resume:
