@@ -113,3 +113,14 @@ def test_memory_plan_matches_the_engine_and_the_8b_layout():
     big = plan_memory(LlamaConfig.llama31_8b(), SlideFSDPConfig(dtype=torch.bfloat16, device="cpu"), world=1)
     assert abs(big["host_master_gb"] - 32.12) < 0.01 and abs(big["host_optimizer_gb"] - 64.24) < 0.01
     assert abs(big["host_grads_gb"] - 16.06) < 0.01
+
+
+def test_quickstart_example_runs_on_cpu():
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, os.path.join(root, "examples", "quickstart.py"), "--steps", "2"],
+                       capture_output=True, text=True, timeout=300, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "step 1: loss" in r.stdout and "model.safetensors" in r.stdout
