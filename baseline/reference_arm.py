@@ -16,6 +16,18 @@ code path):
     transformers 5.x returns a bare tensor;
   * OMP threads as the reference's numa_launch.sh assigns them (rank 0 gets
     the spare cores, the other ranks one control core each);
+  * the random weights are drawn on the CPU, so, as under the reference's own
+    train.py (`from_pretrained(device_map="cpu")`), the GPU holds nothing
+    before SlideFSDP allocates its pool.  This matters: the reference's last
+    decoder layer stays resident between its forward and backward, so its
+    backward fetch returns early (layer_state.py:285-287) without zeroing the
+    pool unit's gradient buffer or pointing `param.grad` at it; the gradient
+    copy to the host (layer_state.py:367-381) then reads a buffer the backward
+    never wrote, and LayerAdam applies it (layer_adam.py:404-417).  On fresh
+    device memory that buffer holds zeros (step 1) or stale gradients of other
+    layers (later steps), so losses stay finite; after a GPU-side random
+    initialisation it held fp32 random bits whose low halves include bf16
+    NaN/Inf patterns, and every loss after the first update was NaN;
   * the same synthetic batches, timing and JSON fields as our own arm.
 """
 from __future__ import annotations
@@ -111,7 +123,7 @@ def run(args, rank, world, local):
 
     dev = torch.device("cuda", local)
     t0 = time.time()
-    model, attn = build_hf_model(args.model, dev)
+    model, attn = build_hf_model(args.model, "cpu")
     cfg = RefConfig(dtype=torch.bfloat16, device=dev, param_transfer_mode=args.param_transfer_mode,
                     grad_sync_mode=args.grad_sync_mode, gpu_buffer_pool_size=args.pool, lr=1e-5,
                     weight_decay=0.01, attention_implementation=attn, ac_offload_mode=args.ac_offload,

@@ -57,6 +57,8 @@ def parse_args():
                    help="shard mode: prefetch each layer with the standalone fused gather instead of "
                         "gathering it inside its QKV GEMM")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-trace-step", action="store_true",
+                   help="skip the traced (untimed) step whose per-phase busy times go into the detail")
     p.add_argument("--profile-json", default="")
     args = p.parse_args()
     given = {a.split("=")[0] for a in sys.argv[1:] if a.startswith("--")}
@@ -258,7 +260,7 @@ def run_ours(args, rank, world, local):
 
     V = mcfg.vocab_size
     g = torch.Generator().manual_seed(1000 + rank)
-    n_batches = args.warmup + 2 * args.steps
+    n_batches = args.warmup + 2 * args.steps + 1
     batches = [torch.randint(0, V, (args.batch, args.seq), generator=g).pin_memory() for _ in range(n_batches)]
     dev_batches = [b.to(dev) for b in batches]
     torch.cuda.synchronize()
@@ -299,6 +301,21 @@ def run_ours(args, rank, world, local):
     adam_busy = (engine.updates.busy_s - adam0) / args.steps
     blocked = (engine.updates.blocked_s - blocked0) / args.steps
 
+    # ---- one traced step after the timed region (untimed): per-phase busy
+    # time of this rank (copy stream, compute, gradient stream, optimizer)
+    phases = None
+    if not args.no_trace_step:
+        engine.wait_for_updates()
+        barrier(world)
+        engine.tracer.start(None)
+        b = dev_batches[-1]
+        losses.append(float(engine(input_ids=b, labels=b).loss))
+        engine.wait_for_updates()
+        rec = engine.tracer.last or {}
+        engine.tracer.stop()
+        phases = {"wall_ms": rec.get("wall_ms"), "phase_ms": rec.get("phase_ms"),
+                  "max_over_ranks_ms": rec.get("max_over_ranks_ms")}
+
     # ---- end-to-end loop through the public API: pinned host batch copied
     # in every step, loss read back every step
     e2e = None
@@ -329,6 +346,7 @@ def run_ours(args, rank, world, local):
         "init_phases_s": dict(engine.init_times),
         "losses": losses, "h2d_gb_per_step": h2d_per_step / 1e9, "adam_busy_s_per_step": adam_busy,
         "fetch_blocked_on_adam_s_per_step": blocked, "comm": engine.comm.name,
+        "traced_step": phases,
     }
 
 
@@ -368,6 +386,9 @@ def main():
         res = run_ours(args, rank, world, local)
 
     res["clocks"] = merge_clocks(res.get("clocks"), world)
+    res["per_rank"] = gather_per_rank(res, world)
+    finite = all_finite(res.get("losses", []), world)
+    res["losses_finite"] = finite
     line = make_line(args, world, res)
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -379,6 +400,42 @@ def main():
 
         dist.barrier()
         dist.destroy_process_group()
+    if not finite and args.impl == "ours":
+        # a diverged run is not a measurement
+        print(f"[rank {rank}] non-finite loss in this run: {res.get('losses')}", file=sys.stderr, flush=True)
+        sys.exit(3)
+
+
+PER_RANK_KEYS = ("h2d_gb_per_step", "adam_busy_s_per_step", "fetch_blocked_on_adam_s_per_step",
+                 "traced_step", "init_s")
+
+
+def gather_per_rank(res: dict, world: int):
+    """Each rank's own step detail (host traffic, optimizer time, per-phase
+    busy time of its traced step), gathered on every rank (a collective)."""
+    mine = {k: res[k] for k in PER_RANK_KEYS if k in res}
+    if world == 1:
+        return [mine]
+    import torch.distributed as dist
+
+    out = [None] * world
+    dist.all_gather_object(out, mine)
+    return out
+
+
+def all_finite(losses, world: int) -> bool:
+    """True when every loss of every rank is finite (a collective)."""
+    import math
+
+    ok = all(isinstance(x, (int, float)) and math.isfinite(x) for x in losses)
+    if world == 1:
+        return ok
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([1.0 if ok else 0.0], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item() > 0)
 
 
 def make_line(args, world: int, res: dict) -> dict:
@@ -420,8 +477,8 @@ def make_line(args, world: int, res: dict) -> dict:
         if args.impl == "fsdp":
             line["config"]["parallelism"] = f"fsdp{world} full_shard, CPU-offloaded params, torch AdamW"
     extra = {k: res[k] for k in ("init_s", "init_phases_s", "h2d_gb_per_step", "adam_busy_s_per_step",
-                                 "fetch_blocked_on_adam_s_per_step", "comm", "losses",
-                                 "attn_implementation") if k in res}
+                                 "fetch_blocked_on_adam_s_per_step", "comm", "losses", "losses_finite",
+                                 "traced_step", "per_rank", "attn_implementation") if k in res}
     line["detail"] = extra
     return line
 

@@ -46,6 +46,20 @@ class PhaseTracer:
         self._host: List[tuple] = []   # (phase, layer, seconds)
         self._lock = threading.Lock()
         self._step_t0 = time.perf_counter()
+        self.last: Optional[dict] = None  # record of the last traced step
+
+    def start(self, path: Optional[str] = None) -> None:
+        """Turn tracing on from the next phase (``path`` None: keep each
+        step's record in ``last`` only, write no file)."""
+        self.path = path
+        self.enabled = True
+        self._dev.clear()
+        with self._lock:
+            self._host.clear()
+        self._step_t0 = time.perf_counter()
+
+    def stop(self) -> None:
+        self.enabled = False
 
     # ------------------------------------------------------------ device
     def begin(self, phase: str, layer: int, stream=None):
@@ -131,6 +145,8 @@ class PhaseTracer:
                 rec["max_over_ranks_ms"] = {n: round(float(x), 3) for n, x in zip(names + ["wall"], t.tolist())}
         if extra:
             rec.update(extra)
-        with open(self.path, "a") as f:
-            f.write(json.dumps(rec) + "\n")
+        self.last = rec
+        if self.path:
+            with open(self.path, "a") as f:
+                f.write(json.dumps(rec) + "\n")
         return rec

@@ -228,3 +228,17 @@ def test_clock_sampler_picks_its_gpu_by_bus_id():
     assert pick(0, (0, 0x1B, 0), table) == 3  # CUDA device 0 is nvidia-smi GPU 3
     assert pick(1, (0, 0x99, 0), table) == 1  # unknown bus: the CUDA index
     assert pick(2, None, table) == 2 and pick(2, (0, 0x18, 0), "") == 2
+
+
+def test_bench_flags_non_finite_losses():
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_fin", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    assert bench.all_finite([12.5, 11.9, 11.0], 1)
+    assert not bench.all_finite([12.5, float("nan")], 1)
+    assert not bench.all_finite([float("inf")], 1)
+    assert bench.gather_per_rank({"h2d_gb_per_step": 1.0, "losses": [1.0]}, 1) == [{"h2d_gb_per_step": 1.0}]
