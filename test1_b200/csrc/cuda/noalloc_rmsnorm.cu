@@ -10,16 +10,8 @@
 // partial-sum workspace on every call; this variant takes the outputs from
 // the caller and keeps its workspace in a fixed file-scope device array.
 //
-//   int t1_rmsnorm_bwd_noalloc(const __nv_bfloat16* dy, const __nv_bfloat16* x,
-//                              const __nv_bfloat16* w, const float* rstd,
-//                              const __nv_bfloat16* residual_grad /* or NULL */,
-//                              __nv_bfloat16* dx, __nv_bfloat16* dw,
-//                              int T, int H, cudaStream_t stream);
-//
-// Computes, for x [T, H] row-major, w [H], rstd [T] (from the forward):
-//   dx = rstd * (dy*w - xhat * mean(dy*w * xhat)) [+ residual_grad],  xhat = x * rstd
-//   dw = sum over rows of dy * xhat
-// All pointers are device pointers; dx/dw are written in full.
+// The prototype, return codes and limits are declared in t1_noalloc.h (the
+// compiler checks this definition against it).
 //
 // Limits: H must be a positive multiple of 8 and at most 8192; T >= 0.
 // The scratch array holds kScratchFloats = 524288 floats (2 MiB).  It is part
@@ -30,7 +22,9 @@
 // Return value: 0 on success; 1 if an argument is invalid (null pointer,
 // T < 0, H not a multiple of 8, or H <= 0); 2 if H exceeds 8192 (the
 // scratch maximum); 3 if the scratch array's device address could not be
-// obtained; otherwise 1000 + the cudaError_t of the failed launch.
+// obtained; 4 if a CUDA error from earlier, unrelated work was already
+// pending on entry (nothing is launched and that error is left for its owner
+// to see); otherwise 1000 + the cudaError_t of the failed launch.
 //
 // Set-up: the first call on each device looks up the scratch array's device
 // address with cudaGetSymbolAddress (with that device current) and caches
@@ -51,6 +45,7 @@
 #include <mutex>
 
 #include "bounds.cuh"
+#include "t1_noalloc.h"
 
 namespace t1 {
 namespace noalloc {
@@ -58,7 +53,7 @@ namespace noalloc {
 using bf16 = __nv_bfloat16;
 
 constexpr int kScratchFloats = 1 << 19;  // 2 MiB
-constexpr int kMaxH = 8192;
+constexpr int kMaxH = T1_NOALLOC_MAX_H;
 constexpr int kThreads = 256;
 constexpr int kMaxDevices = 64;
 
@@ -211,10 +206,13 @@ extern "C" int t1_rmsnorm_bwd_noalloc(const __nv_bfloat16* dy, const __nv_bfloat
   using namespace t1::noalloc;
   if (dy == nullptr || x == nullptr || w == nullptr || rstd == nullptr || dx == nullptr ||
       dw == nullptr || T < 0 || H <= 0 || H % 8 != 0)
-    return 1;
-  if (H > kMaxH) return 2;
+    return T1_NOALLOC_BAD_ARGUMENT;
+  if (H > kMaxH) return T1_NOALLOC_TOO_LARGE;
+  // an error left by earlier work would otherwise be reported (and cleared)
+  // as a failure of these launches
+  if (cudaPeekAtLastError() != cudaSuccess) return T1_NOALLOC_PENDING_ERROR;
   float* scratch = scratch_for_current_device();
-  if (scratch == nullptr) return 3;
+  if (scratch == nullptr) return T1_NOALLOC_NO_SCRATCH;
   const int max_groups = kScratchFloats / H;  // >= 64 since H <= 8192
   int groups = 0;
   if (T > 0) {
@@ -233,12 +231,12 @@ extern "C" int t1_rmsnorm_bwd_noalloc(const __nv_bfloat16* dy, const __nv_bfloat
       default: rows_kernel<4><<<groups, kThreads, 0, stream>>>(dy, x, w, rstd, residual_grad, dx, scratch, T, H, rows); break;
     }
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return 1000 + static_cast<int>(e);
+    if (e != cudaSuccess) return T1_NOALLOC_LAUNCH_ERROR + static_cast<int>(e);
     reduce_kernel<<<(H + 255) / 256, 256, 0, stream>>>(scratch, groups, H, dw);
   } else {
     // no rows: dw is the empty sum
     reduce_kernel<<<(H + 255) / 256, 256, 0, stream>>>(scratch, 0, H, dw);
   }
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : 1000 + static_cast<int>(e);
+  return e == cudaSuccess ? T1_NOALLOC_OK : T1_NOALLOC_LAUNCH_ERROR + static_cast<int>(e);
 }

@@ -124,3 +124,18 @@ def test_quickstart_example_runs_on_cpu():
                        capture_output=True, text=True, timeout=300, cwd=root)
     assert r.returncode == 0, r.stderr[-2000:]
     assert "step 1: loss" in r.stdout and "model.safetensors" in r.stdout
+
+
+def test_cpu_adam_benchmark_profiling_modes():
+    import importlib.util
+    import os
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("cab", os.path.join(root, "benchmark", "cpu_adam_benchmark.py"))
+    cab = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(cab)
+    r = cab.profile_cprofile(10_000, 2, 3, top=5)
+    assert r["mode"] == "cprofile" and r["iters"] == 3 and r["min_ms"] > 0
+    assert "step" in r["profile"]  # LayerAdam.step shows in the cumulative listing
+    p = cab.profile_perf("3B", 1, 1)
+    assert p["mode"] == "perf_stat" and ("counters" in p or "unavailable" in p)
