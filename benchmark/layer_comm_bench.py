@@ -1,11 +1,17 @@
 """Per-layer communication microbenchmark (comparison config 5) for one
 Llama-3.1-8B decoder layer (218,112,000 params, bf16 on the GPU), 2..8 GPUs:
 
-  (a) shard fetch: this rank's 1/N shard of the fp32 master (split layout,
-      page-locked host memory) -> bf16 on every GPU, fused with the QKV GEMM
-      on activations [4096 tokens x 4096]   -- fused_ag_qkv
-      vs. NCCL path: H2D of the fp32 shard + cast + all_gather_into_tensor
-      + cuBLAS QKV GEMM
+  (a) shard fetch: this rank's 1/N shard of the layer's bf16 copy (the high
+      plane of the split master, page-locked host memory) -> the whole layer
+      on every GPU, then the QKV GEMM on activations [4096 tokens x 4096]:
+        staged fused  -- copy-engine H2D of the shard into this rank's unit,
+                         then fused_ag_qkv (NVLink broadcast inside the
+                         tcgen05 QKV GEMM)
+        staged split  -- the same H2D, fused_shard_gather (NVLink broadcast
+                         on 32 CTAs), then the QKV GEMM
+        zero-copy     -- fused_ag_qkv reading the fp32 master (both planes,
+                         4 B/param) from host memory itself
+      vs. NCCL path: H2D of the bf16 shard + all_gather_into_tensor + cuBLAS
   (b) gradient reduce-scatter + 1/N scale + copy into the page-locked host
       shard                                  -- fused_rs_d2h
       vs. NCCL path: reduce_scatter_tensor + scale + D2H copy
@@ -123,19 +129,26 @@ def main():
     x = torch.randn(T, H, device=dev).bfloat16()
     qkv = torch.empty(T, n_qkv, device=dev, dtype=torch.bfloat16)
 
-    def fused_a():
+    def fused_a():  # zero-copy: the kernel reads both master planes from host memory
         C.fused_ag_qkv(x, unit.tensor, n_qkv, qkv, unit.ptrs, unit.sigs, shards, rank, world,
                        hi, lo, unit.next_epoch(), unit.ag_counters)
 
-    f32_dev = torch.empty(ss, device=dev, dtype=torch.float32)
+    def staged_fused_a():
+        unit.tensor[s:e].copy_(hi, non_blocking=True)
+        C.fused_ag_qkv(x, unit.tensor, n_qkv, qkv, unit.ptrs, unit.sigs, shards, rank, world,
+                       unit.tensor[s:e], None, unit.next_epoch(), unit.ag_counters)
+
+    def staged_split_a():
+        unit.tensor[s:e].copy_(hi, non_blocking=True)
+        C.fused_shard_gather(unit.ptrs, unit.sigs, rank, world, s, n, unit.tensor[s:e], None,
+                             unit.next_epoch(), unit.counter, err, 32)
+        C.gemm_bf16(x, unit.tensor[: n_qkv * H].view(n_qkv, H), qkv, False, False, None)
+
     gathered = torch.empty(world * ss, device=dev, dtype=torch.bfloat16)
-    master_f32 = torch.empty(n, dtype=torch.float32, pin_memory=True)
-    _native.host().split_to_f32(hi, lo, master_f32)
 
     def nccl_a():
-        f32_dev[:n].copy_(master_f32, non_blocking=True)
         mine = gathered[rank * ss:(rank + 1) * ss]
-        mine.copy_(f32_dev)
+        mine[:n].copy_(hi, non_blocking=True)
         dist.all_gather_into_tensor(gathered, mine)
         torch.matmul(x, gathered[: n_qkv * H].view(n_qkv, H).t(), out=qkv)
 
@@ -151,6 +164,8 @@ def main():
         grad_host[:n].copy_(rs_out[:n], non_blocking=True)
 
     ta = maxr(timed(fused_a))
+    tsa = maxr(timed(staged_fused_a))
+    tsp = maxr(timed(staged_split_a))
     tna = maxr(timed(nccl_a))
     tb = maxr(timed(fused_b))
     tnb = maxr(timed(nccl_b))
@@ -192,17 +207,21 @@ def main():
     tc = maxr((time.perf_counter() - t0) / 3 * 1e3)
 
     flops = 2.0 * T * n_qkv * H
-    pcie_a = 4.0 * n  # fp32 master bytes (both planes) over this rank's host link
     nvl_a = 2.0 * P * (world - 1) / world  # bf16 bytes each GPU receives from peers
-    roof_a = max(flops / (peak * 1e12), pcie_a / (PCIE_GBS * 1e9), nvl_a / (NVLINK_GBS * 1e9)) * 1e3
+    roof_a = max(flops / (peak * 1e12), 4.0 * n / (PCIE_GBS * 1e9), nvl_a / (NVLINK_GBS * 1e9)) * 1e3
+    # staged: 2 B/param over PCIe; the host leg and the NVLink leg run one after the other here
+    roof_sa = max(flops / (peak * 1e12), 2.0 * n / (PCIE_GBS * 1e9), nvl_a / (NVLINK_GBS * 1e9)) * 1e3
     pcie_b = 2.0 * n
     nvl_b = 2.0 * n * (world - 1)  # each GPU pulls its shard from N-1 peers
     roof_b = max(pcie_b / (PCIE_GBS * 1e9), nvl_b / (NVLINK_GBS * 1e9)) * 1e3
     if rank == 0:
         out = {
             "n_gpus": world, "layer_params": P, "error_word": code,
-            "a_fused_ag_qkv_ms": round(ta, 3), "a_nccl_h2d_allgather_cublas_ms": round(tna, 3),
-            "a_roofline_ms": round(roof_a, 3), "a_frac_of_roofline": round(roof_a / ta, 3),
+            "a_staged_fused_ag_qkv_ms": round(tsa, 3), "a_staged_gather_then_gemm_ms": round(tsp, 3),
+            "a_staged_roofline_ms": round(roof_sa, 3), "a_staged_frac_of_roofline": round(roof_sa / tsa, 3),
+            "a_nccl_h2d_bf16_allgather_cublas_ms": round(tna, 3),
+            "a_zero_copy_fp32_master_fused_ms": round(ta, 3), "a_zero_copy_roofline_ms": round(roof_a, 3),
+            "a_zero_copy_frac_of_roofline": round(roof_a / ta, 3),
             "b_fused_rs_d2h_ms": round(tb, 3), "b_nccl_reduce_scatter_d2h_ms": round(tnb, 3),
             "b_roofline_ms": round(roof_b, 3), "b_frac_of_roofline": round(roof_b / tb, 3),
             "c_layeradam_shard_ms": round(tc, 2),

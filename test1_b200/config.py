@@ -13,8 +13,13 @@ Extra fields (all optional, reference configs never set them):
         default) or "rank0" (the reference's single-optimizer placement).
     fused_comm: use the fused NVLink kernels for shard all-gather and
         gpu_reduce reduce-scatter when available (else NCCL).
-    shard_source: what shard mode reads from host memory: the fp32
-        "master" (cast to bf16 on the GPU) or the bf16 "shadow".
+    shard_source: what shard mode reads from host memory: the bf16
+        "shadow" (default; the high plane of the split master), moved by the
+        copy engine one layer ahead and then broadcast over NVLink, 2 B per
+        parameter over PCIe; or the fp32 "master", read by the gather
+        kernels themselves and rounded to bf16 on the GPU, 4 B per parameter.
+    shard_gather_ctas: CTAs of the NVLink broadcast kernel that runs next to
+        the compute kernels in staged shard mode.
     host_threads: size of the per-rank host worker pool (0 = all CPUs in the
         affinity mask).
     master_layout: how the fp32 master is stored in host memory: "split"
@@ -106,7 +111,8 @@ class SlideFSDPConfig:
     # ---- fields without a reference counterpart --------------------------
     optimizer_sharding: str = "rank"
     fused_comm: bool = True
-    shard_source: str = "master"  # shard fetch reads the fp32 "master" (cast on GPU) or the bf16 "shadow"
+    shard_source: str = "shadow"  # shard fetch reads the bf16 "shadow" (copy engine) or the fp32 "master"
+    shard_gather_ctas: int = 32
     host_threads: int = 0
     host_wait_timeout_s: float = 600.0  # bound on every host wait for a peer rank
     exact_grad_clip: bool = False  # clip to clip_grad_norm before the updates

@@ -44,7 +44,7 @@ void fused_rs_d2h(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t 
 void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t world,
                         int64_t offset, int64_t n, torch::Tensor host_src,
                         c10::optional<torch::Tensor> host_src_lo, int64_t epoch,
-                        torch::Tensor counter, torch::Tensor err);
+                        torch::Tensor counter, torch::Tensor err, int64_t max_ctas);
 void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Tensor out,
                   torch::Tensor ptrs, torch::Tensor sigs, torch::Tensor shards, int64_t rank,
                   int64_t world, torch::Tensor host_src, c10::optional<torch::Tensor> host_src_lo,
@@ -128,7 +128,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_set_mode", &t1::attn_set_mode, "0: mma.sync forward, 1: tcgen05 forward");
   m.def("attn_get_mode", &t1::attn_get_mode);
   m.def("fused_rs_d2h", &t1::fused_rs_d2h);
-  m.def("fused_shard_gather", &t1::fused_shard_gather);
+  m.def("fused_shard_gather", &t1::fused_shard_gather, pybind11::arg("ptrs"), pybind11::arg("sigs"),
+        pybind11::arg("rank"), pybind11::arg("world"), pybind11::arg("offset"), pybind11::arg("n"),
+        pybind11::arg("host_src"), pybind11::arg("host_src_lo"), pybind11::arg("epoch"),
+        pybind11::arg("counter"), pybind11::arg("err"), pybind11::arg("max_ctas") = 0);
   m.def("fused_ag_qkv", &t1::fused_ag_qkv);
   m.def("multi_tensor_adam", &t1::multi_tensor_adam,
         "Adam/AdamW update of lists [grads, params, exp_avgs, exp_avg_sqs] (one launch per 192 tensors)");

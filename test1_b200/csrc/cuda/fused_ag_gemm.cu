@@ -1,11 +1,12 @@
 // Shard-mode layer fetch fused with the first consuming GEMM (the QKV
 // projection), one kernel per layer and rank:
 //
-//   * 2 gather warps per CTA read this rank's shard of the layer from
+//   * 2 gather warps per CTA read this rank's shard of the layer -- from
 //     page-locked host memory (the fp32 master, cast to bf16 in registers,
-//     or the bf16 shadow) and store it into every peer's pool unit over
-//     NVLink (P2P stores; no multicast), then publish per-256-row-block
-//     arrival flags in every peer's signal pad;
+//     or the bf16 shadow), or, in the staged form, from this rank's own unit
+//     where the copy engine placed it one layer ahead -- and store it into
+//     every peer's pool unit over NVLink (P2P stores; no multicast), then
+//     publish per-256-row-block arrival flags in every peer's signal pad;
 //   * the tcgen05 GEMM warps (CTA pairs, cta_group::2, by default; single
 //     CTAs when the GEMM mode is 0) compute qkv = x * W_qkv^T from the *local* unit:
 //     before TMA-loading the B rows of a tile, the producer waits (bounded)
@@ -75,6 +76,15 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
   ag.world = static_cast<int>(world);
   ag.shard_off = shard_off;
   ag.shard_n = shard_n;
+  ag.skip_self = 0;
+  if (host_src.is_cuda()) {
+    // staged form: the shard already sits in this rank's unit
+    TORCH_CHECK(host_src.scalar_type() == torch::kBFloat16 && !(host_src_lo.has_value() && host_src_lo->defined()),
+                "a device-resident shard source must be bf16");
+    TORCH_CHECK(host_src.data_ptr() == static_cast<void*>(static_cast<__nv_bfloat16*>(unit.data_ptr()) + shard_off),
+                "a device-resident shard source must be this rank's unit at the shard offset");
+    ag.skip_self = 1;
+  }
   const void* src = host_src.data_ptr();
   if (host_src.device().is_cpu()) {
     void* d = nullptr;

@@ -9,10 +9,14 @@
 //    reduce_scatter + a device-to-host copy.
 //
 //  * fused_shard_gather: the shard path.  Rank r reads its shard of the
-//    layer's master from page-locked host memory (fp32 master, cast to bf16
-//    here, or the bf16 shadow), and stores it into every peer's pool unit at
-//    the shard offset (P2P stores over NVLink).  One kernel replaces a
-//    host-to-device copy + NCCL all_gather (+ the cast).
+//    layer and stores it into every peer's pool unit at the shard offset
+//    (P2P stores over NVLink).  The source is either page-locked host memory
+//    read zero-copy (fp32 master, cast to bf16 here, or the bf16 shadow) --
+//    one kernel instead of a host-to-device copy + NCCL all_gather (+ the
+//    cast) -- or, in the staged form, the shard already copied into this
+//    rank's own unit by the copy engine: the kernel is then the NVLink
+//    broadcast alone, runs on a few CTAs next to the compute kernels, and
+//    skips the store onto itself.
 //
 // Cross-GPU ordering uses per-buffer signal pads (uint32 slots in each
 // rank's pad, written by peers with release stores at system scope, read
@@ -178,7 +182,8 @@ __device__ __forceinline__ bf16 load1_as_bf16(int kind, const void* src, const v
 __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, int world, long offset,
                                                            long n, int kind, const void* __restrict__ host_src,
                                                            const void* __restrict__ host_src_lo,
-                                                           uint32_t epoch, int* counter, int* err) {
+                                                           int skip_self, uint32_t epoch, int* counter,
+                                                           int* err) {
   // my unit is free (stream order): announce it, wait until every peer's is
   if (blockIdx.x == 0 && threadIdx.x == 0) signal_all(pe, rank, world, epoch);
   const uint32_t* my_pad = reinterpret_cast<const uint32_t*>(pe.sig[rank]);
@@ -189,6 +194,7 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, i
     const int4 out = load8_as_bf16(kind, host_src, host_src_lo, 8 * i);
 #pragma unroll 1
     for (int p = 0; p < world; ++p) {
+      if (skip_self && p == rank) continue;  // the source already is this rank's unit
       bf16* dst = reinterpret_cast<bf16*>(pe.ptr[p]) + offset + 8 * i;
       *reinterpret_cast<int4*>(dst) = out;
     }
@@ -196,7 +202,8 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, i
   if (blockIdx.x == 0) {
     for (long j = (n8 << 3) + threadIdx.x; j < n; j += blockDim.x) {
       const bf16 v = load1_as_bf16(kind, host_src, host_src_lo, j);
-      for (int p = 0; p < world; ++p) reinterpret_cast<bf16*>(pe.ptr[p])[offset + j] = v;
+      for (int p = 0; p < world; ++p)
+        if (!(skip_self && p == rank)) reinterpret_cast<bf16*>(pe.ptr[p])[offset + j] = v;
     }
   }
   finish(pe, rank, world, epoch, counter, err, 212);
@@ -224,9 +231,11 @@ static fused::Peers make_peers(torch::Tensor ptrs, torch::Tensor sigs, int world
   return pe;
 }
 
-static int comm_grid(long n8) {
+// max_ctas > 0 caps the grid (a gather that overlaps compute kernels takes
+// only a few SMs); otherwise up to two CTAs per SM.
+static int comm_grid(long n8, long max_ctas = 0) {
   long want = (n8 + 255) / 256;
-  long cap = 2L * num_sms();
+  long cap = max_ctas > 0 ? max_ctas : 2L * num_sms();
   return static_cast<int>(std::max<long>(1, std::min(want, cap)));
 }
 
@@ -266,15 +275,17 @@ static const void* device_view(const torch::Tensor& t) {
 
 // host_src: this rank's shard: fp32 master, bf16 copy, or (with host_src_lo)
 // the high plane of a split master.
+// host_src on the GPU must be this rank's own unit at [offset, offset + n)
+// (the staged form): the kernel then only broadcasts it to the peers.
 void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, int64_t world,
                         int64_t offset, int64_t n, torch::Tensor host_src,
                         c10::optional<torch::Tensor> host_src_lo, int64_t epoch,
-                        torch::Tensor counter, torch::Tensor err) {
+                        torch::Tensor counter, torch::Tensor err, int64_t max_ctas) {
   auto pe = make_peers(ptrs, sigs, world);
   if (n <= 0) {
     // empty share: still take part in the per-epoch handshake (one CTA)
     fused::shard_gather_kernel<<<1, 256, 0, stream()>>>(pe, rank, world, offset, 0, fused::kSrcBf16,
-                                                        nullptr, nullptr, static_cast<uint32_t>(epoch),
+                                                        nullptr, nullptr, 0, static_cast<uint32_t>(epoch),
                                                         counter.data_ptr<int>(), err.data_ptr<int>());
     check_launch("fused_shard_gather");
     count_launch();
@@ -298,9 +309,16 @@ void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, in
     TORCH_CHECK(host_src.scalar_type() == torch::kBFloat16, "host_src must be fp32 or bf16");
     kind = fused::kSrcBf16;
   }
-  fused::shard_gather_kernel<<<comm_grid(n / 8), 256, 0, stream()>>>(
-      pe, rank, world, offset, n, kind, device_view(host_src), lo, static_cast<uint32_t>(epoch),
-      counter.data_ptr<int>(), err.data_ptr<int>());
+  int skip_self = 0;
+  if (host_src.is_cuda()) {
+    TORCH_CHECK(kind == fused::kSrcBf16, "a device-resident shard source must be bf16");
+    TORCH_CHECK(reinterpret_cast<uint64_t>(host_src.data_ptr()) == pe.ptr[rank] + 2 * static_cast<uint64_t>(offset),
+                "a device-resident shard source must be this rank's own unit at the shard offset");
+    skip_self = 1;
+  }
+  fused::shard_gather_kernel<<<comm_grid(n / 8, max_ctas), 256, 0, stream()>>>(
+      pe, rank, world, offset, n, kind, device_view(host_src), lo, skip_self,
+      static_cast<uint32_t>(epoch), counter.data_ptr<int>(), err.data_ptr<int>());
   check_launch("fused_shard_gather");
   count_launch();
 }

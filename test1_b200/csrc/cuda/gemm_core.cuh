@@ -48,6 +48,8 @@ struct AgParams {
   const void* host_src;        // device view of the page-locked shard
   const void* host_src_lo;     // split master: the low plane
   int src_kind;                // 0 bf16 copy, 1 fp32 master, 2 split master (hi/lo planes)
+  int skip_self;               // the source is this rank's own unit (placed there by the copy
+                               // engine): store to the peers only
   uint32_t epoch;
   int n_blocks;                // 256-row blocks of B (= the QKV weight rows / 256)
   long block_elems;            // 256 * K
@@ -119,8 +121,10 @@ __device__ __forceinline__ void ag_copy(const AgParams& ag, long b, long e, int 
 #pragma unroll
       for (int k = 0; k < 4; ++k) o[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
     }
-    for (int q = 0; q < ag.world; ++q)
+    for (int q = 0; q < ag.world; ++q) {
+      if (ag.skip_self && q == ag.rank) continue;
       *reinterpret_cast<int4*>(reinterpret_cast<bf16*>(ag.peer[q]) + 8 * v) = out;
+    }
   }
 }
 
@@ -189,7 +193,8 @@ __device__ __forceinline__ void ag_gather_warps(const AgParams& ag, const ErrorS
                                 static_cast<const uint16_t*>(ag.host_src_lo)[local]) - 0x8000u;
             v = __float2bfloat16_rn(__uint_as_float(b));
           }
-          for (int q = 0; q < ag.world; ++q) reinterpret_cast<bf16*>(ag.peer[q])[j] = v;
+          for (int q = 0; q < ag.world; ++q)
+            if (!(ag.skip_self && q == ag.rank)) reinterpret_cast<bf16*>(ag.peer[q])[j] = v;
         }
       }
       __threadfence_system();

@@ -99,6 +99,15 @@ class CommStrategy:
         layer ``st`` (the engine page-locks exactly these)."""
         return [st.shadow]
 
+    def h2d_bytes(self, st: LayerRuntimeState, element_size: int) -> int:
+        """Bytes one ``fetch_params`` of ``st`` moves over this rank's host link."""
+        return st.numel * element_size
+
+    def fetch_host_leg(self, st: LayerRuntimeState, dst: torch.Tensor, stream: Stream) -> bool:
+        """Only the host-to-device part of a shard fetch (strategies that
+        stage it); False when the strategy has none."""
+        return False
+
     def sync_grads(self, st: LayerRuntimeState, src: torch.Tensor, stream: Stream) -> None:
         """Enqueue on ``stream`` everything that moves this rank's share of
         the layer gradient into ``st.grad_host``."""
@@ -157,6 +166,12 @@ class CollectiveComm(CommStrategy):
             return super().host_read_views(st)
         s, e = shard_bounds(st.numel, self.world, self.rank)
         return [st.shadow[s:e]] if e > s else []
+
+    def h2d_bytes(self, st: LayerRuntimeState, element_size: int) -> int:
+        if self.param_mode == "full":
+            return super().h2d_bytes(st, element_size)
+        s, e = shard_bounds(st.numel, self.world, self.rank)
+        return max(0, e - s) * element_size
 
     def fetch_params(self, st: LayerRuntimeState, dst: torch.Tensor, stream: Stream) -> None:
         if self.param_mode == "full":

@@ -13,9 +13,16 @@ engine's hot paths:
                NVLink (P2P loads from every peer's unit), scaled by 1/N,
                rounded to bf16 and stored directly into this rank's
                page-locked host gradient shard (zero-copy).
-  shard        ``fused_shard_gather``: this rank's shard of the layer master
-               is read from page-locked host memory (fp32, cast on the GPU),
-               and stored into every peer's unit (P2P stores over NVLink).
+  shard        staged (default, ``shard_source="shadow"``): the copy engine
+               moves this rank's shard of the layer's bf16 copy (the high
+               plane of the split master, 2 B/param) into its own unit, then
+               ``fused_shard_gather`` broadcasts it into every peer's unit
+               (P2P stores over NVLink) on a few CTAs, one layer ahead of
+               use, like full mode's prefetch; or the broadcast runs inside
+               the layer's QKV GEMM (``fused_ag_qkv``, ``fuse_gather_qkv``).
+               ``shard_source="master"``: the kernels read the fp32 master
+               (both planes, 4 B/param) from page-locked host memory
+               themselves and round it to bf16 on the GPU.
 
 Buffers keep a per-buffer epoch counter (identical on every rank because the
 schedule is); kernels signal and wait on it with bounded waits and report
@@ -86,8 +93,9 @@ class FusedComm(CollectiveComm):
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
         self.fused_grads = self.grad_mode == "gpu_reduce" and not self.rank0_optimizer
         self.fused_params = self.param_mode == "shard"
-        src = getattr(config, "shard_source", "master")
-        self.shard_source = src if src in ("master", "shadow") else "master"
+        src = getattr(config, "shard_source", "shadow")
+        self.shard_source = src if src in ("master", "shadow") else "shadow"
+        self.gather_ctas = int(getattr(config, "shard_gather_ctas", 32))
 
     def disable_fused(self, params: bool, grads: bool) -> None:
         """Fall back to the NCCL path for parameter gathers and/or gradient
@@ -124,15 +132,50 @@ class FusedComm(CollectiveComm):
         return 1.0 if self.fused_grads else 1.0 / self.world
 
     # operations ----------------------------------------------------------
+    @property
+    def staged(self) -> bool:
+        """Shard fetches move the host leg with the copy engine (bf16 copy)."""
+        return self.fused_params and self.shard_source == "shadow"
+
+    def fetch_host_leg(self, st: LayerRuntimeState, dst: torch.Tensor, stream: Stream) -> bool:
+        """Staged shard mode: enqueue on ``stream`` the copy-engine transfer of
+        this rank's shard of the layer's bf16 copy into its own unit.  Returns
+        False (nothing enqueued) when shard fetches are not staged."""
+        if not self.staged:
+            return False
+        s, e = shard_bounds(st.numel, self.world, self.rank)
+        if e > s:
+            with stream.ctx():
+                dst[s:e].copy_(st.shadow[s:e], non_blocking=True)
+        return True
+
     def fetch_params(self, st: LayerRuntimeState, dst: torch.Tensor, stream: Stream) -> None:
         if not self.fused_params:
             return super().fetch_params(st, dst, stream)
         s, e = shard_bounds(st.numel, self.world, self.rank)
         b = self._buf(dst)
+        if self.fetch_host_leg(st, dst, stream):
+            # NVLink leg on a few CTAs: the shard, now in this rank's unit,
+            # into every peer's
+            with stream.ctx():
+                _native.cuda().fused_shard_gather(b.ptrs, b.sigs, self.rank, self.world, s, e - s,
+                                                  dst[s:e] if e > s else dst[:0], None, b.next_epoch(),
+                                                  b.counter, self.err, self.gather_ctas)
+            return
         src, lo = self._gather_src(st, s, e)
         with stream.ctx():
             _native.cuda().fused_shard_gather(b.ptrs, b.sigs, self.rank, self.world, s, e - s,
                                               src, lo, b.next_epoch(), b.counter, self.err)
+
+    def h2d_bytes(self, st: LayerRuntimeState, element_size: int) -> int:
+        """Bytes one parameter fetch of ``st`` moves over this rank's host link."""
+        if not self.fused_params:
+            return super().h2d_bytes(st, element_size)
+        s, e = shard_bounds(st.numel, self.world, self.rank)
+        if self.staged:
+            return 2 * max(0, e - s)
+        src, lo = self._gather_src(st, s, e)
+        return max(0, e - s) * (4 if (lo is not None or src.element_size() == 4) else 2)
 
     def host_read_views(self, st: LayerRuntimeState) -> list:
         if not self.fused_params:
@@ -140,6 +183,8 @@ class FusedComm(CollectiveComm):
         s, e = shard_bounds(st.numel, self.world, self.rank)
         if e <= s:
             return []
+        if self.staged:
+            return [st.shadow[s:e]]
         return [t for t in self._gather_src(st, s, e) if t is not None]
 
     def sync_grads(self, st: LayerRuntimeState, src: torch.Tensor, stream: Stream) -> None:
@@ -192,10 +237,15 @@ class FusedComm(CollectiveComm):
 
     def ag_qkv(self, st: LayerRuntimeState, x1: torch.Tensor, n_rows: int) -> torch.Tensor:
         """Gather layer ``st`` into every rank's unit and return x1 @ W_qkv^T
-        (one kernel, on the current stream)."""
+        (one kernel, on the current stream).  Staged: the shard already sits
+        in this rank's unit (``fetch_host_leg``), so the kernel's gather warps
+        read it from local memory and only push it to the peers."""
         s, e = shard_bounds(st.numel, self.world, self.rank)
         b = self._buf(st.unit.param)
-        src, lo = self._gather_src(st, s, e)
+        if self.staged:
+            src, lo = st.unit.param[s:e], None
+        else:
+            src, lo = self._gather_src(st, s, e)
         out = torch.empty(x1.shape[0], n_rows, dtype=x1.dtype, device=x1.device)
         _native.cuda().fused_ag_qkv(x1, b.tensor, n_rows, out, b.ptrs, b.sigs,
                                     self.shard_table(st.numel), self.rank, self.world, src, lo,

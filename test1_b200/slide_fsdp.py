@@ -617,8 +617,12 @@ class SlideFSDP(nn.Module):
     def _update_target(self, st: LayerRuntimeState) -> int:
         return self.comm.updaters_for(st.numel) * self.completed_steps
 
-    def _fetch(self, st: LayerRuntimeState, with_grad: bool, need_weights: bool = True) -> None:
-        """Acquire a pool unit for ``st`` and enqueue its parameter load."""
+    def _fetch(self, st: LayerRuntimeState, with_grad: bool, need_weights: bool = True,
+               host_leg_only: bool = False) -> None:
+        """Acquire a pool unit for ``st`` and enqueue its parameter load.
+        ``host_leg_only``: staged shard mode with the gather fused into the
+        QKV GEMM -- enqueue only the copy-engine transfer of this rank's
+        shard; the layer's fused kernel broadcasts it."""
         if st.resident:
             if with_grad:
                 st.bind_device(with_grad=True)
@@ -632,9 +636,13 @@ class SlideFSDP(nn.Module):
             self.tracer.host("wait_update", st.idx, time.perf_counter() - t0)
             self.h2d_stream.wait(unit.free_event)
             tok = self.tracer.begin("h2d", st.idx, self.h2d_stream)
-            self.comm.fetch_params(st, unit.param, self.h2d_stream)
+            if host_leg_only:
+                self.comm.fetch_host_leg(st, unit.param, self.h2d_stream)
+                st.gather_pending = True
+            else:
+                self.comm.fetch_params(st, unit.param, self.h2d_stream)
             self.tracer.end(tok)
-            self.h2d_bytes += st.numel * unit.param.element_size()
+            self.h2d_bytes += self.comm.h2d_bytes(st, unit.param.element_size())
             st.loaded = self.h2d_stream.record()
         else:
             st.loaded = unit.free_event
@@ -651,7 +659,7 @@ class SlideFSDP(nn.Module):
             torch.cuda.current_stream(self.device).wait_event(unit.free_event.e)
         st.loaded = None
         st.bind_device(with_grad=False)
-        self.h2d_bytes += st.numel * unit.param.element_size()
+        self.h2d_bytes += self.comm.h2d_bytes(st, unit.param.element_size())
 
     def _check_unit(self, st: LayerRuntimeState, where: str) -> None:
         """Debug aid (env T1_CHECK_FETCH=1): compare the device copy of a
@@ -673,12 +681,16 @@ class SlideFSDP(nn.Module):
 
     def _early_weight(self, st: LayerRuntimeState, name: str) -> torch.Tensor:
         """One small parameter of layer ``st`` on the device ahead of the
-        layer's fused gather: read from the shared fp32 master and rounded to
-        the compute dtype (nearest even) exactly as the gather kernel rounds
-        it, so the forward and the backward recompute agree."""
+        layer's fused gather, with exactly the values the gather delivers (so
+        the forward and the backward recompute agree): the bf16 copy when the
+        fetch is staged, else the fp32 master rounded to nearest even as the
+        gather kernel rounds it."""
         for e in st.layout.entries:
             if e.name == name:
-                w = st.store.read_fp32(e.offset, e.offset + e.numel).to(self.dtype).view(e.shape)
+                if getattr(self.comm, "staged", False):
+                    w = st.shadow[e.offset:e.offset + e.numel].view(e.shape)
+                else:
+                    w = st.store.read_fp32(e.offset, e.offset + e.numel).to(self.dtype).view(e.shape)
                 if not self.is_cuda:
                     return w
                 # through page-locked staging (torch's caching host allocator
@@ -839,8 +851,13 @@ class SlideFSDP(nn.Module):
         fuse_first = (L > 0 and not self.generic and hasattr(self.comm, "can_fuse_qkv")
                       and self.comm.can_fuse_qkv(S[1]) and self.config.use_native_kernels
                       and self.config.fuse_gather_qkv)
-        if L > 0 and not fuse_first:
-            self._fetch(S[1], with_grad=False)
+        # staged + fused: the copy engine brings this rank's shard of layer
+        # i+1 into its unit while layer i computes; layer i+1's QKV kernel
+        # then only pushes it to the peers
+        staged = fuse_first and getattr(self.comm, "staged", False)
+        prefetching = not fuse_first or staged
+        if L > 0 and prefetching:
+            self._fetch(S[1], with_grad=False, host_leg_only=staged)
         self._wait_loaded(emb)
         self._check_unit(emb, "forward")
         with self.tracer.span("fwd", 0):
@@ -855,15 +872,16 @@ class SlideFSDP(nn.Module):
             st = S[i]
             qkv_fn = None
             ln1 = None
-            if fuse_qkv:
+            if fuse_qkv and (getattr(st, "gather_pending", False) or not st.resident):
                 # shard mode: the layer is gathered by its own fused QKV kernel;
                 # the input norm ahead of it gets its weight separately
-                if not st.resident:
-                    self._acquire_unloaded(st)
-                    qkv_fn = (lambda x1, st=st: self.comm.ag_qkv(st, x1, n_qkv))
-                    ln1 = self._early_weight(st, "input_layernorm.weight")
+                if staged:
+                    self._wait_loaded(st)  # this rank's shard is in the unit
                 else:
-                    self._wait_loaded(st)
+                    self._acquire_unloaded(st)
+                st.gather_pending = False
+                qkv_fn = (lambda x1, st=st: self.comm.ag_qkv(st, x1, n_qkv))
+                ln1 = self._early_weight(st, "input_layernorm.weight")
             else:
                 self._wait_loaded(st)
             tok = self.tracer.begin("fwd", i)
@@ -874,17 +892,17 @@ class SlideFSDP(nn.Module):
                 h, saved_all[i] = st.module.forward_train(h, ctx, save=True, qkv_fn=qkv_fn, ln1_weight=ln1)
             self.tracer.end(tok)
             self._check_unit(st, "forward")
-            if not fuse_qkv:
+            if prefetching:
                 # prefetch the next layer(s) into free units
                 for j in range(i + 1, min(i + prefetch, L) + 1):
                     if not S[j].resident and S[j].pool.num_free:
-                        self._fetch(S[j], with_grad=False)
+                        self._fetch(S[j], with_grad=False, host_leg_only=staged)
             if i == L:
                 self._fetch(out, with_grad=True)
             else:
                 self._release(st, Event(dev).record())
-            if not fuse_qkv and i + 1 <= L and not S[i + 1].resident:
-                self._fetch(S[i + 1], with_grad=False)
+            if prefetching and i + 1 <= L and not S[i + 1].resident:
+                self._fetch(S[i + 1], with_grad=False, host_leg_only=staged)
         if L == 0:
             self._fetch(out, with_grad=True)
 

@@ -79,6 +79,18 @@ def kernels(rank, world, port, out_path):
             if not torch.equal(pbuf.tensor.cpu(), master.bfloat16()):
                 ok = False
                 msgs.append(f"gather it{it} mismatch")
+            # staged: this rank's shard already in its own unit (copy
+            # engine), the kernel only broadcasts it, on a capped grid
+            pbuf.tensor.zero_()
+            torch.cuda.synchronize()
+            dist.barrier()
+            pbuf.tensor[s:e].copy_(master.bfloat16()[s:e], non_blocking=True)
+            C.fused_shard_gather(pbuf.ptrs, pbuf.sigs, rank, world, s, e - s, pbuf.tensor[s:e], None,
+                                 pbuf.next_epoch(), pbuf.counter, err, 4)
+            torch.cuda.synchronize()
+            if not torch.equal(pbuf.tensor.cpu(), master.bfloat16()):
+                ok = False
+                msgs.append(f"staged gather it{it} mismatch")
         if int(err.item()) != 0:
             ok = False
             msgs.append(f"err {int(err.item())}")
@@ -91,7 +103,7 @@ def kernels(rank, world, port, out_path):
         raise
 
 
-def engine(rank, world, port, out_path, mode, fused):
+def engine(rank, world, port, out_path, mode, fused, extra=None):
     try:
         _init(rank, world, port)
         from test1_b200 import SlideFSDPConfig
@@ -104,7 +116,8 @@ def engine(rank, world, port, out_path, mode, fused):
         model = LlamaForCausalLM(cfg)
         eng = SlideFSDP(model, SlideFSDPConfig(dtype=torch.bfloat16, device=torch.device("cuda", rank),
                                                lr=1e-3, param_transfer_mode=mode,
-                                               grad_sync_mode="gpu_reduce", fused_comm=fused))
+                                               grad_sync_mode="gpu_reduce", fused_comm=fused,
+                                               **(extra or {})))
         g = torch.Generator().manual_seed(11)
         losses = []
         for step in range(3):
@@ -148,7 +161,9 @@ def ag_gemm(rank, world, port, out_path, src_kind):
         for it in range(3):
             master = torch.randn(P, generator=torch.Generator().manual_seed(31 + it)) * 0.05
             lo = None
-            if src_kind == "split":
+            if src_kind == "staged":
+                src = unit.tensor[s:e]  # filled below, after the zero fill
+            elif src_kind == "split":
                 hi_all = torch.empty(P, dtype=torch.bfloat16)
                 lo_all = torch.empty(P, dtype=torch.int16)
                 _native.host().f32_to_split(master, hi_all, lo_all)
@@ -159,6 +174,8 @@ def ag_gemm(rank, world, port, out_path, src_kind):
             x = torch.randn(T, K, generator=torch.Generator().manual_seed(77 + it)).bfloat16().to(dev)
             out = torch.empty(T, n_rows, dtype=torch.bfloat16, device=dev)
             unit.tensor.zero_()
+            if src_kind == "staged":
+                unit.tensor[s:e].copy_(master.bfloat16()[s:e])
             torch.cuda.synchronize()
             dist.barrier()
             C.fused_ag_qkv(x, unit.tensor, n_rows, out, unit.ptrs, unit.sigs, shards, rank, world,

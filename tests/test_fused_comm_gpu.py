@@ -47,14 +47,26 @@ def test_fused_kernels_two_gpus(tmp_path):
         assert res["ok"], res["msgs"]
 
 
-@pytest.mark.parametrize("mode", ["full", "shard"])
-def test_engine_fused_matches_nccl(tmp_path, mode):
+# shard variants: staged fetch (copy engine + NVLink broadcast) with the
+# broadcast fused into the QKV GEMM or prefetched on its own, and the
+# zero-copy fp32-master source
+SHARD_VARIANTS = {
+    "full": ("full", {}),
+    "shard": ("shard", {}),
+    "shard-prefetch": ("shard", {"fuse_gather_qkv": False}),
+    "shard-master": ("shard", {"shard_source": "master"}),
+}
+
+
+@pytest.mark.parametrize("variant", list(SHARD_VARIANTS))
+def test_engine_fused_matches_nccl(tmp_path, variant):
     _need2()
     from tests._fused_worker import engine
 
+    mode, extra = SHARD_VARIANTS[variant]
     a = str(tmp_path / "fused")
     b = str(tmp_path / "nccl")
-    _run(engine, (_port(), a, mode, True), tmp_path)
+    _run(engine, (_port(), a, mode, True, extra), tmp_path)
     _run(engine, (_port(), b, mode, False), tmp_path)
     fa, fb = torch.load(a + ".0"), torch.load(b + ".0")
     assert fa["comm"] == "fused-nvlink" and fb["comm"] == "collective"
@@ -73,7 +85,7 @@ def test_engine_fused_matches_nccl(tmp_path, mode):
     assert not bad, "\n".join(bad)
 
 
-@pytest.mark.parametrize("src_kind", ["fp32", "bf16", "split"])
+@pytest.mark.parametrize("src_kind", ["fp32", "bf16", "split", "staged"])
 def test_fused_ag_qkv_two_gpus(tmp_path, src_kind):
     _need2()
     from tests._fused_worker import ag_gemm
