@@ -245,6 +245,10 @@ class SlideFSDP(nn.Module):
             if creator:
                 self.shared.unlink()
         self.counters = self.shared.view(torch.uint8, self._ctr_off, 8 * n_counters)
+        # step-entry heartbeat: counter[base + r] = steps rank r has started,
+        # counter[base + 32 + r] = 1 + the steps rank r completed before it
+        # left (0 while it is still training)
+        self._live_base = 4 * self.num_layers
         phase("shared_region")
 
         # ---- comm strategy (needs the slot region for cpu_reduce)
@@ -834,11 +838,39 @@ class SlideFSDP(nn.Module):
         if bool((m[:, 1:] & ~m[:, :-1]).any()):
             raise NotImplementedError("only right-padded attention masks are supported")
 
+    def _enter_step(self, step: int) -> None:
+        """Announce that this rank starts ``step`` and wait (bounded by
+        ``host_wait_timeout_s``) until every other rank has started it too,
+        before any GPU work or collective of the step is issued.  A rank that
+        closed its engine is reported at once; one that stopped without
+        closing is reported when the wait expires.  Either way the error
+        names the rank, and nothing of this step is in flight on the GPU."""
+        if self.world_size == 1 or self.world_size > 32:
+            return
+        host = _native.host()
+        base = self._live_base
+        host.counter_add(self.counters, base + self.rank, 1)
+        timeout = float(self.config.host_wait_timeout_s)
+        deadline = time.monotonic() + timeout
+        for r in range(self.world_size):
+            if r == self.rank:
+                continue
+            while host.counter_load(self.counters, base + r) < step:
+                left = int(host.counter_load(self.counters, base + 32 + r))
+                if left:
+                    raise RankLeftError(f"rank {r} left the run after step {left - 1}; rank {self.rank} "
+                                        f"cannot start step {step}")
+                if time.monotonic() > deadline:
+                    raise TimeoutError(f"rank {r} did not start step {step} within {timeout:.1f}s "
+                                       f"(it stalled or died); rank {self.rank} stops before the step")
+                host.counter_wait_geq(self.counters, base + r, step, 0.05)
+
     @torch.no_grad()
     def _train_step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         cfg = self.model_config
         dev = self.device
         step = self.completed_steps + 1
+        self._enter_step(step)
         if self.cpu_slots is not None:
             self.cpu_slots.step = step
         ctx = self._make_context(input_ids, labels)
@@ -1170,6 +1202,10 @@ class SlideFSDP(nn.Module):
             self.wait_for_updates()
         except Exception as exc:  # closing still releases everything; say what was lost
             warnings.warn(f"SlideFSDP.close: pending optimizer updates did not complete: {exc}")
+        if 1 < self.world_size <= 32:
+            # tell the other ranks at their next step that this one is gone
+            _native.host().counter_add(self.counters, self._live_base + 32 + self.rank,
+                                       self.completed_steps + 1)
         self.updates.close()
         if self._reducer is not None:
             self._reducer.close()
@@ -1190,6 +1226,10 @@ class SlideFSDP(nn.Module):
             self.close()
         except Exception:
             pass
+
+
+class RankLeftError(RuntimeError):
+    """Another rank of the run closed its engine; this rank cannot continue."""
 
 
 class _SubRegion:

@@ -40,6 +40,24 @@ def test_dead_rank_detected_by_survivor(tmp_path, grad_mode):
             or "peer" in msg or "gloo" in msg), r0["error"]
 
 
+def test_closed_rank_reported_at_next_step(tmp_path):
+    """A rank that closes its engine between steps is named at once by the
+    others' next step (no timeout needed)."""
+    out = str(tmp_path / "res")
+    ctx = mp.get_context("spawn")
+    port = _port()
+    ps = [ctx.Process(target=run, args=(r, 2, port, out, "gpu_reduce", "close")) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout=240)
+    r0 = torch.load(out + ".0")
+    assert torch.load(out + ".1").get("left")
+    assert r0["error"] is not None and r0["error"].startswith("RankLeftError"), r0["error"]
+    assert "rank 1 left the run after step 1" in r0["error"], r0["error"]
+    assert r0["steps"] == 1
+
+
 def test_update_wait_timeout_names_layer():
     from test1_b200.runtime.host_memory import HostRegion
     from test1_b200.runtime.update import UpdateScheduler
