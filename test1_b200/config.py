@@ -20,6 +20,9 @@ Extra fields (all optional, reference configs never set them):
         kernels themselves and rounded to bf16 on the GPU, 4 B per parameter.
     shard_gather_ctas: CTAs of the NVLink broadcast kernel that runs next to
         the compute kernels in staged shard mode.
+    lm_head_chunk_tokens: the output layer computes lm_head + cross-entropy
+        and their gradients in chunks of this many tokens (only a
+        [chunk, vocab] logits buffer exists); 0 keeps the full logits.
     host_threads: size of the per-rank host worker pool (0 = all CPUs in the
         affinity mask).
     master_layout: how the fp32 master is stored in host memory: "split"
@@ -113,6 +116,7 @@ class SlideFSDPConfig:
     fused_comm: bool = True
     shard_source: str = "shadow"  # shard fetch reads the bf16 "shadow" (copy engine) or the fp32 "master"
     shard_gather_ctas: int = 32
+    lm_head_chunk_tokens: int = 2048
     host_threads: int = 0
     host_wait_timeout_s: float = 600.0  # bound on every host wait for a peer rank
     exact_grad_clip: bool = False  # clip to clip_grad_norm before the updates
@@ -150,6 +154,8 @@ class SlideFSDPConfig:
             raise ValueError(f"master_layout must be 'split', 'fp32' or 'bf16', got {self.master_layout}")
         if self.optimizer_state_dtype not in ("fp32", "bf16"):
             raise ValueError(f"optimizer_state_dtype must be 'fp32' or 'bf16', got {self.optimizer_state_dtype}")
+        if self.lm_head_chunk_tokens < 0:
+            raise ValueError(f"lm_head_chunk_tokens must be >= 0, got {self.lm_head_chunk_tokens}")
         if self.shard_source not in ("master", "shadow"):
             raise ValueError(f"shard_source must be 'master' or 'shadow', got {self.shard_source}")
         if self.gpu_buffer_pool_size < 2:

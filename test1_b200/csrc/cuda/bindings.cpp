@@ -23,6 +23,9 @@ torch::Tensor swiglu_fwd(torch::Tensor gu);
 torch::Tensor swiglu_bwd(torch::Tensor da, torch::Tensor gu);
 torch::Tensor embedding_fwd(torch::Tensor ids, torch::Tensor w);
 void embedding_bwd(torch::Tensor dh, torch::Tensor ids, torch::Tensor dw);
+std::vector<torch::Tensor> linear_cross_entropy(torch::Tensor x, torch::Tensor w, torch::Tensor targets,
+                                                torch::Tensor dx, torch::Tensor dw, int64_t chunk_rows,
+                                                int64_t ignore_index);
 std::vector<torch::Tensor> cross_entropy_fwd_bwd(torch::Tensor logits, torch::Tensor targets,
                                                  int64_t ignore_index, double grad_scale);
 void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, bool b_mn,
@@ -117,6 +120,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_fwd", &t1::embedding_fwd);
   m.def("embedding_bwd", &t1::embedding_bwd);
   m.def("cross_entropy_fwd_bwd", &t1::cross_entropy_fwd_bwd);
+  m.def("linear_cross_entropy", &t1::linear_cross_entropy,
+        "chunked lm_head GEMM + cross-entropy forward/backward: (loss, count); writes dx and dW");
   m.def("gemm_bf16", &t1::gemm_bf16, pybind11::arg("A"), pybind11::arg("B"), pybind11::arg("C"),
         pybind11::arg("a_mn"), pybind11::arg("b_mn"), pybind11::arg("R") = pybind11::none());
   m.def("gemm_check_error", &t1::gemm_check_error, pybind11::arg("reset") = false);

@@ -1,8 +1,12 @@
-// Embedding gather / deterministic scatter-add and the fused
-// cross-entropy forward + backward on sm_100a.
+// Embedding gather / deterministic scatter-add, the fused cross-entropy
+// forward + backward, and the chunked linear cross-entropy of the output
+// layer on sm_100a.
 #include "common.cuh"
 
 namespace t1 {
+
+void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, bool b_mn,
+               c10::optional<torch::Tensor> R);
 
 using bf16 = __nv_bfloat16;
 
@@ -187,6 +191,65 @@ std::vector<torch::Tensor> cross_entropy_fwd_bwd(torch::Tensor logits, torch::Te
                                                   loss.data_ptr<float>());
   check_launch("ce_loss_reduce");
   count_launch(3);
+  return {loss, count};
+}
+
+// Output layer of a causal LM without the [T, V] logits: for each chunk of
+// `chunk_rows` tokens, logits = x_c W^T into one reusable [chunk_rows, V]
+// buffer (tcgen05 GEMM), the cross-entropy forward + backward overwrites
+// them with d(loss)/d(logits) (mean over the valid targets of the WHOLE
+// batch, counted once up front), then dx_c = dlogits W and
+// dW (+)= dlogits^T x_c -- the first chunk stores dW, later ones add to it
+// through the GEMM's residual epilogue.  Peak extra memory: chunk_rows x V
+// bf16 (the reference gets the same effect from Liger's fused linear
+// cross-entropy, slide_fsdp.py:86-98).  Returns (loss [1] fp32, count [1]).
+std::vector<torch::Tensor> linear_cross_entropy(torch::Tensor x, torch::Tensor w, torch::Tensor targets,
+                                                torch::Tensor dx, torch::Tensor dw, int64_t chunk_rows,
+                                                int64_t ignore_index) {
+  T1_CHECK_INPUT(x, torch::kBFloat16);
+  T1_CHECK_INPUT(w, torch::kBFloat16);
+  T1_CHECK_INPUT(dx, torch::kBFloat16);
+  T1_CHECK_INPUT(dw, torch::kBFloat16);
+  TORCH_CHECK(targets.is_cuda() && targets.scalar_type() == torch::kInt64, "targets must be int64 CUDA");
+  TORCH_CHECK(x.dim() == 2 && x.is_contiguous() && w.dim() == 2 && w.is_contiguous(),
+              "x [T, H] and w [V, H] must be contiguous");
+  const int64_t T = x.size(0), H = x.size(1), V = w.size(0);
+  TORCH_CHECK(w.size(1) == H && V % 8 == 0 && H % 8 == 0, "w must be [V, H] with V, H multiples of 8");
+  TORCH_CHECK(dx.sizes() == x.sizes() && dx.is_contiguous(), "dx must be contiguous [T, H]");
+  TORCH_CHECK(dw.sizes() == w.sizes() && dw.is_contiguous(), "dw must be contiguous [V, H]");
+  TORCH_CHECK(targets.numel() == T, "targets must have T entries");
+  TORCH_CHECK(chunk_rows > 0, "chunk_rows must be positive");
+  auto tg = targets.contiguous();
+  auto opts = x.options();
+  auto count = torch::empty({1}, opts.dtype(torch::kInt32));
+  auto row_loss = torch::empty({std::max<int64_t>(T, 1)}, opts.dtype(torch::kFloat32));
+  auto loss = torch::empty({1}, opts.dtype(torch::kFloat32));
+  count_valid_kernel<<<1, 1024, 0, stream()>>>(tg.data_ptr<int64_t>(), T, ignore_index, count.data_ptr<int>());
+  check_launch("count_valid");
+  count_launch();
+  if (T == 0) {
+    dw.zero_();
+  } else {
+    const int64_t rows_max = std::min(chunk_rows, T);
+    auto buf = torch::empty({rows_max, V}, opts);
+    for (int64_t t0 = 0; t0 < T; t0 += rows_max) {
+      const int64_t rows = std::min(rows_max, T - t0);
+      auto L = buf.narrow(0, 0, rows);
+      auto xc = x.narrow(0, t0, rows);
+      gemm_bf16(xc, w, L, false, false, c10::nullopt);  // logits
+      ce_fwd_bwd_kernel<<<rows, 512, 0, stream()>>>((bf16*)L.data_ptr(), tg.data_ptr<int64_t>() + t0, V,
+                                                     ignore_index, -1.f, count.data_ptr<int>(),
+                                                     row_loss.data_ptr<float>() + t0);
+      check_launch("ce_fwd_bwd (chunk)");
+      count_launch();
+      gemm_bf16(L, w, dx.narrow(0, t0, rows), false, true, c10::nullopt);  // dx = dlogits W
+      gemm_bf16(L, xc, dw, true, true, t0 == 0 ? c10::optional<torch::Tensor>() : c10::optional<torch::Tensor>(dw));
+    }
+  }
+  ce_loss_reduce_kernel<<<1, 1024, 0, stream()>>>(row_loss.data_ptr<float>(), T, count.data_ptr<int>(),
+                                                  loss.data_ptr<float>());
+  check_launch("ce_loss_reduce");
+  count_launch();
   return {loss, count};
 }
 

@@ -196,13 +196,15 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, boo
     if (add) launch<false, false, gemm::kAddResidual>(ta, tb, p);
     else launch<false, false, gemm::kStore>(ta, tb, p);
   } else if (!a_mn && b_mn) {
-    TORCH_CHECK(!add, "residual epilogue is only built for the forward layout");
+    TORCH_CHECK(!add, "residual epilogue is built for the forward and wgrad layouts");
     launch<false, true, gemm::kStore>(ta, tb, p);
   } else if (a_mn && b_mn) {
-    TORCH_CHECK(!add, "residual epilogue is only built for the forward layout");
-    launch<true, true, gemm::kStore>(ta, tb, p);
+    // wgrad; with R == C it accumulates (the chunked linear cross-entropy
+    // sums its weight gradient over token chunks this way)
+    if (add) launch<true, true, gemm::kAddResidual>(ta, tb, p);
+    else launch<true, true, gemm::kStore>(ta, tb, p);
   } else {
-    TORCH_CHECK(!add, "residual epilogue is only built for the forward layout");
+    TORCH_CHECK(!add, "residual epilogue is built for the forward and wgrad layouts");
     launch<true, false, gemm::kStore>(ta, tb, p);
   }
 }

@@ -88,6 +88,13 @@ def cross_entropy_fwd_bwd(logits, targets, ignore_index=-100, grad_scale=None):
     return _impl(logits).cross_entropy_fwd_bwd(logits, targets, ignore_index, grad_scale)
 
 
+def linear_cross_entropy(x, w, targets, dx, dw, chunk_rows, ignore_index=-100):
+    """Output layer's lm_head GEMM + cross-entropy forward and backward in
+    token chunks (no [T, V] logits kept): writes dx [T, H] and dw [V, H],
+    returns (loss fp32 scalar, n_valid)."""
+    return _impl(x).linear_cross_entropy(x, w, targets, dx, dw, chunk_rows, ignore_index)
+
+
 shift_labels = reference.shift_labels
 rope_tables = reference.rope_tables
 

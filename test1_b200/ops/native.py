@@ -126,6 +126,12 @@ def embedding_bwd(dh, ids, num_rows, out=None):
     return out
 
 
+# ----------------------------------------------- chunked linear cross-entropy
+def linear_cross_entropy(x, w, targets, dx, dw, chunk_rows, ignore_index=-100):
+    loss, count = _c().linear_cross_entropy(x, w, targets, dx, dw, int(chunk_rows), int(ignore_index))
+    return loss.reshape(()), count
+
+
 # ------------------------------------------------------------ cross-entropy
 def cross_entropy_fwd_bwd(logits, targets, ignore_index=-100, grad_scale=None):
     """Overwrites ``logits`` with the gradient; returns (loss [] fp32 on the

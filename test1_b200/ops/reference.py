@@ -243,6 +243,32 @@ def cross_entropy_fwd_bwd(logits: torch.Tensor, targets: torch.Tensor, ignore_in
     return loss, p.to(logits.dtype), n_valid
 
 
+def linear_cross_entropy(x: torch.Tensor, w: torch.Tensor, targets: torch.Tensor, dx: torch.Tensor,
+                         dw: torch.Tensor, chunk_rows: int, ignore_index: int = -100):
+    """Output layer without the [T, V] logits: mean cross-entropy of
+    logits = x w^T over targets != ignore_index, processed in chunks of
+    ``chunk_rows`` tokens.  Writes dx = dlogits w and dw = dlogits^T x (in
+    fp32 arithmetic, rounded once into their dtype); returns (loss fp32
+    scalar, n_valid)."""
+    T = x.shape[0]
+    valid = targets != ignore_index
+    n_valid = int(valid.sum())
+    scale = 1.0 / max(n_valid, 1)
+    wf = w.float()
+    dw32 = torch.zeros_like(wf)
+    total = torch.zeros((), dtype=torch.float32, device=x.device)
+    for t0 in range(0, T, max(1, chunk_rows)):
+        t1 = min(T, t0 + chunk_rows)
+        xc = x[t0:t1].float()
+        logits = xc @ wf.t()
+        loss_c, dl, n_c = cross_entropy_fwd_bwd(logits, targets[t0:t1], ignore_index, grad_scale=scale)
+        total = total + loss_c * n_c  # loss_c is the chunk's mean over its n_c valid targets
+        dx[t0:t1].copy_(dl @ wf)
+        dw32 += dl.t() @ xc
+    dw.copy_(dw32)
+    return total / max(n_valid, 1), n_valid
+
+
 # ------------------------------------------------ fused-layout entry points
 # The model keeps q/k/v as column blocks of one [T, (Hq + 2 Hkv) * D] buffer
 # and gate/up as the two halves of one [T, 2 I] buffer; these wrappers state

@@ -75,13 +75,21 @@ except Exception:  # pragma: no cover
 
 class OutputLayer(nn.Module):
     """Final norm + lm_head moved as one unit (reference slide_fsdp.py:45-113).
-    ``named_parameters``: norm.weight, lm_head.weight."""
+    ``named_parameters``: norm.weight, lm_head.weight.
 
-    def __init__(self, norm: nn.Module, lm_head: nn.Module, eps: float):
+    With ``chunk_tokens`` > 0 (the default, from
+    ``SlideFSDPConfig.lm_head_chunk_tokens``) the lm_head GEMM, the
+    cross-entropy and both gradients run in chunks of that many tokens, so
+    only a [chunk_tokens, V] logits buffer ever exists -- the role of
+    Liger's fused linear cross-entropy in the reference
+    (slide_fsdp.py:86-98); 0 materialises the full [T, V] logits."""
+
+    def __init__(self, norm: nn.Module, lm_head: nn.Module, eps: float, chunk_tokens: int = 0):
         super().__init__()
         self.norm = norm
         self.lm_head = lm_head
         self.eps = eps
+        self.chunk_tokens = int(chunk_tokens)
 
     def _grads(self):
         for p in self.parameters():
@@ -93,13 +101,17 @@ class OutputLayer(nn.Module):
         """Forward + loss + backward of this layer.  Returns (loss, dh)."""
         w_n, w_lm = self.norm.weight.data, self.lm_head.weight.data
         x, rstd = ops.rmsnorm_fwd(h, w_n, self.eps)
-        logits = ops.linear_fwd(x, w_lm)
-        loss, dlogits, _ = ops.cross_entropy_fwd_bwd(logits, ctx.targets)
-        del logits
         g_n, g_lm = self._grads()
-        dx = ops.linear_dgrad(dlogits, w_lm)
-        ops.linear_wgrad(dlogits, x, out=g_lm)
-        del dlogits
+        if self.chunk_tokens > 0:
+            dx = torch.empty_like(x)
+            loss, _ = ops.linear_cross_entropy(x, w_lm, ctx.targets, dx, g_lm, self.chunk_tokens)
+        else:
+            logits = ops.linear_fwd(x, w_lm)
+            loss, dlogits, _ = ops.cross_entropy_fwd_bwd(logits, ctx.targets)
+            del logits
+            dx = ops.linear_dgrad(dlogits, w_lm)
+            ops.linear_wgrad(dlogits, x, out=g_lm)
+            del dlogits
         dh, dw = ops.rmsnorm_bwd(dx, h, w_n, rstd)
         g_n.copy_(dw)
         return loss, dh
@@ -504,7 +516,7 @@ class SlideFSDP(nn.Module):
             self.embed_tokens = model.get_input_embeddings()
             self.decoder_layers = nn.ModuleList(layers)
             self.output_layer = OutputLayer(decoder.norm, model.get_output_embeddings(),
-                                            model.config.rms_norm_eps)
+                                            model.config.rms_norm_eps, self.config.lm_head_chunk_tokens)
             return
         self.embed_tokens = generic.GenericEmbedding(model.get_input_embeddings())
         self.decoder_layers = nn.ModuleList(generic.GenericDecoderLayer(l) for l in layers)

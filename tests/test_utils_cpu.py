@@ -139,3 +139,21 @@ def test_cpu_adam_benchmark_profiling_modes():
     assert "step" in r["profile"]  # LayerAdam.step shows in the cumulative listing
     p = cab.profile_perf("3B", 1, 1)
     assert p["mode"] == "perf_stat" and ("counters" in p or "unavailable" in p)
+
+
+def test_reference_linear_cross_entropy_chunks_agree_with_full_logits():
+    import torch
+
+    from test1_b200.ops import reference as ref
+
+    T, H, V = 37, 16, 64
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(T, H, generator=g)
+    w = torch.randn(V, H, generator=g) * 0.1
+    t = torch.randint(0, V, (T,), generator=g)
+    t[::5] = -100
+    dx, dw = torch.empty(T, H), torch.empty(V, H)
+    loss, n = ref.linear_cross_entropy(x, w, t, dx, dw, 8)
+    l_full, dl, n_full = ref.cross_entropy_fwd_bwd(x @ w.t(), t)
+    assert n == n_full and abs(float(loss) - float(l_full)) < 1e-5
+    assert torch.allclose(dx, dl @ w, atol=1e-6) and torch.allclose(dw, dl.t() @ x, atol=1e-6)
