@@ -1,6 +1,8 @@
 """One GEMM shape, a few launches: the small case for an ncu capture of the
 tcgen05 GEMM (Llama-3.1-8B QKV projection: 4096 x 6144 x 4096, ~130 MB of
-operands).  Usage: python benchmark/gemm_profile_case.py [fwd|dgrad|wgrad] [--pair]"""
+operands).  Usage: python benchmark/gemm_profile_case.py [fwd|dgrad|wgrad] [--pair | --pair-tma]
+(--pair: CTA pairs with the register-store epilogue; --pair-tma: CTA pairs
+with the shared-memory + TMA-store epilogue)."""
 import os
 import sys
 
@@ -12,7 +14,9 @@ from test1_b200.ops import native  # noqa: E402
 
 def main() -> None:
     kind = sys.argv[1] if len(sys.argv) > 1 and not sys.argv[1].startswith("--") else "fwd"
-    if "--pair" in sys.argv:
+    if "--pair-tma" in sys.argv:
+        native.gemm_set_mode(2)
+    elif "--pair" in sys.argv:
         native.gemm_set_mode(1)
     M, N, K = 4096, 6144, 4096
     x = torch.randn(M, K, device="cuda").bfloat16()

@@ -41,7 +41,7 @@ def peaks():
         return 1590.0, 6650.0, "of fallback"
 
 
-def bench_gemm(T=4096, H=4096, I=14336, nq=32, nkv=8, D=128, modes=(0, 1)):
+def bench_gemm(T=4096, H=4096, I=14336, nq=32, nkv=8, D=128, modes=(0, 1, 2)):
     tf_peak, _, tag = peaks()
     out = []
     shapes = {
@@ -67,7 +67,8 @@ def bench_gemm(T=4096, H=4096, I=14336, nq=32, nkv=8, D=128, modes=(0, 1)):
             dg = timeit(lambda: native.gemm(dy, w, dx, False, True))
             wg = timeit(lambda: native.gemm(dy, x, dw, True, True))
             for kind, t, tc in (("fwd", ours, cub), ("dgrad", dg, dgc), ("wgrad", wg, wgc)):
-                out.append({"kernel": f"gemm_{name}_{kind}", "mode": "pair" if mode else "single",
+                out.append({"kernel": f"gemm_{name}_{kind}",
+                            "mode": {0: "single", 1: "pair", 2: "pair_tma_store"}[mode],
                             "M": M, "N": N, "K": K, "ms": round(t, 4),
                             "tflops": round(fl / t / 1e9, 1), "frac_peak": round(fl / t / 1e9 / tf_peak, 3),
                             "peak_ref": tag, "cublas_ms": round(tc, 4), "vs_cublas": round(tc / t, 3)})

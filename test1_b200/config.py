@@ -115,7 +115,7 @@ class SlideFSDPConfig:
     optimizer_sharding: str = "rank"
     fused_comm: bool = True
     shard_source: str = "shadow"  # shard fetch reads the bf16 "shadow" (copy engine) or the fp32 "master"
-    shard_gather_ctas: int = 32
+    shard_gather_ctas: int = 64
     lm_head_chunk_tokens: int = 2048
     host_threads: int = 0
     host_wait_timeout_s: float = 600.0  # bound on every host wait for a peer rank

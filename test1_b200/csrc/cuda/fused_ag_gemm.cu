@@ -129,23 +129,35 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
   p.ldr = 0;
   p.k_blocks = (K + gemm::BK - 1) / gemm::BK;
   p.err = gemm_error_word().data_ptr<int>();
-  if (gemm_get_mode() == 1) {
+  if (gemm_get_mode() >= 1) {
     // CTA pairs: 256 x 256 tiles, the B row blocks match the arrival flags
     p.tiles_m = (M + gemm::PAIR_BM - 1) / gemm::PAIR_BM;
     p.tiles_n = (n_rows + gemm::PAIR_BN - 1) / gemm::PAIR_BN;
     p.num_tiles = p.tiles_m * p.tiles_n;
     CUtensorMap ta = make_map(x.data_ptr(), K, M, x.stride(0), gemm::PAIR_HALF);
     CUtensorMap tb = make_map(unit.data_ptr(), K, n_rows, K, gemm::PAIR_HALF);
-    auto kern = gemm::gemm_pair_kernel<false, false, gemm::kStore, true>;
-    static bool pair_configured = false;
-    if (!pair_configured) {
-      T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         gemm::PAIR_SMEM_BYTES));
-      pair_configured = true;
-    }
     // every CTA gathers, so the grid spans all SMs even when tiles are few
     const int clusters = num_sms() / 2;
-    kern<<<2 * clusters, 256, gemm::PAIR_SMEM_BYTES, stream()>>>(ta, tb, p, ag);
+    if (gemm_get_mode() == 2) {
+      CUtensorMap tc = make_map(out.data_ptr(), n_rows, M, out.stride(0), 32);
+      auto kern = gemm::gemm_pair_kernel<false, false, gemm::kStore, true, true>;
+      static bool tma_configured = false;
+      if (!tma_configured) {
+        T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           gemm::PAIR_SMEM_BYTES_TMA));
+        tma_configured = true;
+      }
+      kern<<<2 * clusters, 256, gemm::PAIR_SMEM_BYTES_TMA, stream()>>>(ta, tb, p, ag, tc, tc);
+    } else {
+      auto kern = gemm::gemm_pair_kernel<false, false, gemm::kStore, true, false>;
+      static bool pair_configured = false;
+      if (!pair_configured) {
+        T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           gemm::PAIR_SMEM_BYTES));
+        pair_configured = true;
+      }
+      kern<<<2 * clusters, 256, gemm::PAIR_SMEM_BYTES, stream()>>>(ta, tb, p, ag, ta, ta);
+    }
     check_launch("fused_ag_qkv (pair)");
     count_launch();
     return;

@@ -190,13 +190,22 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, i
   if (!block_wait(my_pad, 0, world, epoch, err, 211)) return;
   const long n8 = n >> 3;
   const long stride = static_cast<long>(gridDim.x) * blockDim.x;
-  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
-    const int4 out = load8_as_bf16(kind, host_src, host_src_lo, 8 * i);
+  // kU vectors per thread in flight: the loads (local HBM or PCIe) are
+  // issued together before the peer stores, so latency overlaps
+  constexpr int kU = 4;
+  for (long i0 = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i0 < n8; i0 += kU * stride) {
+    int4 out[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+      if (i0 + u * stride < n8) out[u] = load8_as_bf16(kind, host_src, host_src_lo, 8 * (i0 + u * stride));
 #pragma unroll 1
     for (int p = 0; p < world; ++p) {
       if (skip_self && p == rank) continue;  // the source already is this rank's unit
-      bf16* dst = reinterpret_cast<bf16*>(pe.ptr[p]) + offset + 8 * i;
-      *reinterpret_cast<int4*>(dst) = out;
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const long i = i0 + u * stride;
+        if (i < n8) *reinterpret_cast<int4*>(reinterpret_cast<bf16*>(pe.ptr[p]) + offset + 8 * i) = out[u];
+      }
     }
   }
   if (blockIdx.x == 0) {

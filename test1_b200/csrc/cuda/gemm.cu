@@ -29,8 +29,10 @@
 //
 // Pair mode (gemm_pair.cuh, cta_group::2): CTA pairs compute 256 x 256
 // tiles with one MMA stream, each CTA staging half of the operands.  The
-// mode is chosen per process: gemm_set_mode(0 = single CTA, 1 = pairs), or
-// the environment variable T1_GEMM_PAIR (default: pairs).
+// mode is chosen per process: gemm_set_mode(0 = single CTA, 1 = pairs with
+// register-store epilogue, 2 = pairs with shared-memory + TMA-store
+// epilogue), or the environment variable T1_GEMM_MODE (T1_GEMM_PAIR=0 still
+// selects the single-CTA kernel).
 #include "gemm_core.cuh"
 #include "gemm_pair.cuh"
 
@@ -38,6 +40,8 @@
 
 namespace t1 {
 
+// GEMM mode when neither T1_GEMM_MODE nor T1_GEMM_PAIR is set.
+constexpr int kDefaultGemmMode = 1;
 
 // ================================================================ host side
 T1_BOUNDS_READER(gemm)
@@ -94,38 +98,44 @@ torch::Tensor& gemm_error_word() {
 
 static int& gemm_mode() {
   static int mode = [] {
+    const char* m = std::getenv("T1_GEMM_MODE");
+    if (m != nullptr && m[0] >= '0' && m[0] <= '2' && m[1] == 0) return m[0] - '0';
     const char* e = std::getenv("T1_GEMM_PAIR");
-    return (e != nullptr && e[0] == '0') ? 0 : 1;  // pairs unless T1_GEMM_PAIR=0
+    return (e != nullptr && e[0] == '0') ? 0 : kDefaultGemmMode;
   }();
   return mode;
 }
 
 void gemm_set_mode(int64_t mode) {
-  TORCH_CHECK(mode == 0 || mode == 1, "GEMM mode must be 0 (single CTA) or 1 (CTA pairs)");
+  TORCH_CHECK(mode >= 0 && mode <= 2,
+              "GEMM mode must be 0 (single CTA), 1 (CTA pairs) or 2 (CTA pairs, TMA-store epilogue)");
   gemm_mode() = static_cast<int>(mode);
 }
 
 int64_t gemm_get_mode() { return gemm_mode(); }
 
-template <bool A_MN, bool B_MN, int EPI>
-static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p) {
-  auto kern = gemm::gemm_pair_kernel<A_MN, B_MN, EPI>;
+template <bool A_MN, bool B_MN, int EPI, bool TMA_EPI>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p,
+                        const CUtensorMap& tc, const CUtensorMap& tr) {
+  auto kern = gemm::gemm_pair_kernel<A_MN, B_MN, EPI, false, TMA_EPI>;
+  constexpr int smem = TMA_EPI ? gemm::PAIR_SMEM_BYTES_TMA : gemm::PAIR_SMEM_BYTES;
   static bool configured = false;
   if (!configured) {
-    T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       gemm::PAIR_SMEM_BYTES));
+    T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
   const int clusters = std::min(p.num_tiles, num_sms() / 2);
   gemm::AgParams none{};
-  kern<<<2 * clusters, 192, gemm::PAIR_SMEM_BYTES, stream()>>>(ta, tb, p, none);
+  kern<<<2 * clusters, 192, smem, stream()>>>(ta, tb, p, none, tc, tr);
   check_launch("gemm_bf16 (pair)");
   count_launch();
 }
 
 template <bool A_MN, bool B_MN, int EPI>
-static void launch(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p) {
-  if (gemm_mode() == 1) return launch_pair<A_MN, B_MN, EPI>(ta, tb, p);
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p,
+                   const CUtensorMap& tc, const CUtensorMap& tr) {
+  if (gemm_mode() == 1) return launch_pair<A_MN, B_MN, EPI, false>(ta, tb, p, tc, tr);
+  if (gemm_mode() == 2) return launch_pair<A_MN, B_MN, EPI, true>(ta, tb, p, tc, tr);
   auto kern = gemm::gemm_bf16_kernel<A_MN, B_MN, EPI, false>;
   static bool configured = false;
   if (!configured) {
@@ -163,7 +173,7 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, boo
     else C.zero_();
     return;
   }
-  const bool pair = gemm_mode() == 1;
+  const bool pair = gemm_mode() >= 1;
   CUtensorMap ta = a_mn ? make_map(A.data_ptr(), M, K, A.stride(0), 64)
                         : make_map(A.data_ptr(), K, M, A.stride(0), pair ? gemm::PAIR_HALF : gemm::BM);
   CUtensorMap tb = b_mn ? make_map(B.data_ptr(), N, K, B.stride(0), 64)
@@ -192,20 +202,26 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, boo
     p.R = reinterpret_cast<const bf16*>(R->data_ptr());
     p.ldr = R->stride(0);
   }
+  // output / residual maps of the TMA-store epilogue: 64 x 32 boxes
+  CUtensorMap tc{}, tr{};
+  if (gemm_mode() == 2) {
+    tc = make_map(C.data_ptr(), N, M, C.stride(0), 32);
+    tr = add ? make_map(R->data_ptr(), N, M, R->stride(0), 32) : tc;
+  }
   if (!a_mn && !b_mn) {
-    if (add) launch<false, false, gemm::kAddResidual>(ta, tb, p);
-    else launch<false, false, gemm::kStore>(ta, tb, p);
+    if (add) launch<false, false, gemm::kAddResidual>(ta, tb, p, tc, tr);
+    else launch<false, false, gemm::kStore>(ta, tb, p, tc, tr);
   } else if (!a_mn && b_mn) {
     TORCH_CHECK(!add, "residual epilogue is built for the forward and wgrad layouts");
-    launch<false, true, gemm::kStore>(ta, tb, p);
+    launch<false, true, gemm::kStore>(ta, tb, p, tc, tr);
   } else if (a_mn && b_mn) {
     // wgrad; with R == C it accumulates (the chunked linear cross-entropy
     // sums its weight gradient over token chunks this way)
-    if (add) launch<true, true, gemm::kAddResidual>(ta, tb, p);
-    else launch<true, true, gemm::kStore>(ta, tb, p);
+    if (add) launch<true, true, gemm::kAddResidual>(ta, tb, p, tc, tr);
+    else launch<true, true, gemm::kStore>(ta, tb, p, tc, tr);
   } else {
     TORCH_CHECK(!add, "residual epilogue is built for the forward and wgrad layouts");
-    launch<true, false, gemm::kStore>(ta, tb, p);
+    launch<true, false, gemm::kStore>(ta, tb, p, tc, tr);
   }
 }
 

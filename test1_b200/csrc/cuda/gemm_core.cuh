@@ -91,39 +91,56 @@ __device__ __forceinline__ void ag_signal_all(const AgParams& ag, int slot) {
 }
 __device__ __forceinline__ void ag_named_barrier() { asm volatile("bar.sync 1, 64;" ::: "memory"); }
 
-// Copy elements [b, e) of the layer (inside this rank's shard) from host to
-// every peer, 8 elements per thread per step, 64 gather threads per CTA.
+// 8 elements of this rank's shard at `local` as bf16 (cast from the fp32
+// master or rebuilt from split planes when the source is not bf16).
+__device__ __forceinline__ int4 ag_load8(const AgParams& ag, long local) {
+  int4 out;
+  if (ag.src_kind == 0) {
+    out = *reinterpret_cast<const int4*>(static_cast<const bf16*>(ag.host_src) + local);
+  } else {
+    float f[8];
+    if (ag.src_kind == 1) {
+      const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(ag.host_src) + local);
+      float4 x = src[0], y = src[1];
+      f[0] = x.x; f[1] = x.y; f[2] = x.z; f[3] = x.w;
+      f[4] = y.x; f[5] = y.y; f[6] = y.z; f[7] = y.w;
+    } else {
+      int4 hv = *reinterpret_cast<const int4*>(static_cast<const uint16_t*>(ag.host_src) + local);
+      int4 lv = *reinterpret_cast<const int4*>(static_cast<const uint16_t*>(ag.host_src_lo) + local);
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(&hv);
+      const uint16_t* l = reinterpret_cast<const uint16_t*>(&lv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        f[k] = __uint_as_float(((static_cast<uint32_t>(h[k]) << 16) | l[k]) - 0x8000u);
+    }
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) o[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+  }
+  return out;
+}
+
+// Copy elements [b, e) of the layer (inside this rank's shard) to every peer,
+// 8 elements per vector, 64 gather threads per CTA, 4 vectors per thread in
+// flight (loads issued together ahead of the peer stores).
 __device__ __forceinline__ void ag_copy(const AgParams& ag, long b, long e, int gt) {
   const long v0 = b >> 3, v1 = e >> 3;
-  for (long v = v0 + gt; v < v1; v += 64) {
-    int4 out;
-    const long local = 8 * v - ag.shard_off;
-    if (T1_OOB(local, ag.shard_n) || T1_OOB(local + 7, ag.shard_n)) continue;
-    if (ag.src_kind == 0) {
-      out = *reinterpret_cast<const int4*>(static_cast<const bf16*>(ag.host_src) + local);
-    } else {
-      float f[8];
-      if (ag.src_kind == 1) {
-        const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(ag.host_src) + local);
-        float4 x = src[0], y = src[1];
-        f[0] = x.x; f[1] = x.y; f[2] = x.z; f[3] = x.w;
-        f[4] = y.x; f[5] = y.y; f[6] = y.z; f[7] = y.w;
-      } else {
-        int4 hv = *reinterpret_cast<const int4*>(static_cast<const uint16_t*>(ag.host_src) + local);
-        int4 lv = *reinterpret_cast<const int4*>(static_cast<const uint16_t*>(ag.host_src_lo) + local);
-        const uint16_t* h = reinterpret_cast<const uint16_t*>(&hv);
-        const uint16_t* l = reinterpret_cast<const uint16_t*>(&lv);
+  constexpr int kU = 4;
+  for (long vb = v0 + gt; vb < v1; vb += 64 * kU) {
+    int4 out[kU];
+    bool ok[kU];
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          f[k] = __uint_as_float(((static_cast<uint32_t>(h[k]) << 16) | l[k]) - 0x8000u);
-      }
-      __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(&out);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) o[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+    for (int u = 0; u < kU; ++u) {
+      const long v = vb + 64 * u;
+      const long local = 8 * v - ag.shard_off;
+      ok[u] = v < v1 && !T1_OOB(local, ag.shard_n) && !T1_OOB(local + 7, ag.shard_n);
+      if (ok[u]) out[u] = ag_load8(ag, local);
     }
     for (int q = 0; q < ag.world; ++q) {
       if (ag.skip_self && q == ag.rank) continue;
-      *reinterpret_cast<int4*>(reinterpret_cast<bf16*>(ag.peer[q]) + 8 * v) = out;
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        if (ok[u]) *reinterpret_cast<int4*>(reinterpret_cast<bf16*>(ag.peer[q]) + 8 * (vb + 64 * u)) = out[u];
     }
   }
 }

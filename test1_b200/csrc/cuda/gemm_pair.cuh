@@ -14,6 +14,18 @@
 //   tfull[a]   per CTA; accumulator a finished (commit to both)
 //   tempty[a]  leader's; the 4 epilogue warps of each CTA arrive (count 8)
 // No TMA load uses multicast.
+//
+// Epilogue forms:
+//   register stores (TMA_EPI = false): each thread rounds its row of the
+//     accumulator and stores it with 16-byte global stores (32 rows per warp
+//     instruction);
+//   TMA stores (TMA_EPI = true): each epilogue warp owns two 4 KB shared
+//     buffers of 32 rows x 64 columns in the 128B-swizzled layout; per
+//     64-column slab it reads the accumulator from TMEM, adds the residual
+//     (TMA-loaded into the same buffer), rounds to bf16 into the buffer and
+//     issues one bulk tensor store, double-buffered against the next slab.
+//     The accumulator is handed back to the MMA warp as soon as its last
+//     TMEM load finished, before the stores complete.
 #pragma once
 
 #include "gemm_core.cuh"
@@ -29,25 +41,32 @@ constexpr int PAIR_A_BYTES = PAIR_HALF * BK * 2;
 constexpr int PAIR_B_BYTES = PAIR_HALF * BK * 2;
 constexpr int PAIR_STAGE_BYTES = PAIR_A_BYTES + PAIR_B_BYTES;
 constexpr int PAIR_SMEM_BYTES = PAIR_STAGES * PAIR_STAGE_BYTES + 1024 + 256;
+constexpr int PAIR_EPI_BUF = 32 * 64 * 2;                      // one 32 x 64 bf16 slab: 4 KB
+constexpr int PAIR_EPI_BYTES = 4 /*warps*/ * 2 * PAIR_EPI_BUF;  // 32 KB
+constexpr int PAIR_SMEM_BYTES_TMA = PAIR_SMEM_BYTES + PAIR_EPI_BYTES;
+static_assert(PAIR_SMEM_BYTES_TMA <= 232448, "pair GEMM with TMA epilogue exceeds 227 KB of shared memory");
 
 // AG = true: the shard-mode fused all-gather variant (see gemm_core.cuh and
 // fused_ag_gemm.cu): two more warps per CTA copy this rank's host shard of
 // the layer into every peer's unit, and the producers wait for the B rows
 // of a tile to arrive before loading them.
-template <bool A_MN, bool B_MN, int EPI, bool AG = false>
+template <bool A_MN, bool B_MN, int EPI, bool AG = false, bool TMA_EPI = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
-                     const __grid_constant__ CUtensorMap tma_b, const Params p, const AgParams ag) {
+                     const __grid_constant__ CUtensorMap tma_b, const Params p, const AgParams ag,
+                     const __grid_constant__ CUtensorMap tma_c, const __grid_constant__ CUtensorMap tma_r) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + PAIR_STAGES * PAIR_A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + PAIR_STAGES * PAIR_B_BYTES);
+  uint8_t* sE = sB + PAIR_STAGES * PAIR_B_BYTES;  // epilogue buffers (TMA_EPI), 1024-aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + (TMA_EPI ? PAIR_EPI_BYTES : 0));
   uint64_t* empty = full + PAIR_STAGES;
   uint64_t* tfull = empty + PAIR_STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* rbar = tempty + 2;  // [4] residual loads of the TMA epilogue, one per warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -66,12 +85,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 8);  // 4 epilogue warps x 2 CTAs
     }
+    for (int w = 0; w < 4; ++w) mbar_init(&rbar[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&tma_a);
     prefetch_tensormap(&tma_b);
+    if (TMA_EPI) {
+      prefetch_tensormap(&tma_c);
+      if (EPI == kAddResidual) prefetch_tensormap(&tma_r);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, TMEM_COLS);
@@ -185,6 +209,107 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
     }
   } else if (AG && warp >= 6) {
     ag_gather_warps(ag, err, abort_flag);
+  } else if (TMA_EPI) {
+    // ------------------------------------------- epilogue (TMA stores)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint8_t* wbuf = sE + q * 2 * PAIR_EPI_BUF;
+    const uint32_t leader_tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint32_t leader_tempty1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    uint32_t rphase = 0;
+    int bi = 0;
+    int local = 0;
+    for (int tile = cluster; tile < p.num_tiles; tile += nclusters, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      int ok = 0;
+      if (lane == 0) {
+        ok = !*abort_flag;
+        if (ok && !mbar_wait(&tfull[acc], acc_phase)) {
+          err.set(114);
+          *abort_flag = 1;
+          ok = 0;
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      tc_fence_after();
+      int mb, nb;
+      raster(tile, p.tiles_m, p.tiles_n, mb, nb);
+      const int row0 = mb * PAIR_BM + static_cast<int>(crank) * PAIR_HALF + q * 32;
+      bool failed = false;
+#pragma unroll 1
+      for (int c = 0; c < PAIR_BN; c += 64) {
+        uint8_t* buf = wbuf + bi * PAIR_EPI_BUF;
+        const int col0 = nb * PAIR_BN + c;
+        const bool live = col0 < p.N && row0 < p.M;  // a slab wholly outside C is skipped
+        // the store issued from this buffer two slabs ago has read it
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        if (EPI == kAddResidual && live && lane == 0) {
+          mbar_arrive_expect_tx(&rbar[q], PAIR_EPI_BUF);
+          tma_load_2d(buf, &tma_r, &rbar[q], col0, row0);
+        }
+        uint32_t r0[32], r1[32];
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * PAIR_BN + c;
+        tmem_ld_32x32b_x32(taddr, r0);
+        tmem_ld_32x32b_x32(taddr + 32, r1);
+        tmem_ld_wait();
+        if (c + 64 == PAIR_BN) {
+          // every TMEM read of this accumulator is done: hand it back now
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+        }
+        if (EPI == kAddResidual && live) {
+          int okr = 0;
+          if (lane == 0) okr = mbar_wait(&rbar[q], rphase);
+          rphase ^= 1;
+          if (!__shfl_sync(0xffffffffu, okr, 0)) {
+            if (lane == 0) {
+              err.set(116);
+              *abort_flag = 1;
+            }
+            failed = true;
+            break;
+          }
+        }
+        if (live) {
+          uint8_t* rowp = buf + lane * 128;  // row `lane` of the slab
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4* slot = reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4));
+            float f[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) f[k] = __uint_as_float(j < 4 ? r0[8 * j + k] : r1[8 * (j - 4) + k]);
+            if (EPI == kAddResidual) {
+              uint4 rv = *slot;
+              const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                const float2 t = __bfloat1622float2(rh[k]);
+                f[2 * k] += t.x;
+                f[2 * k + 1] += t.y;
+              }
+            }
+            uint4 ov;
+            __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) oh[k] = __floats2bfloat162_rn(f[2 * k], f[2 * k + 1]);
+            *slot = ov;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tma_c, buf, col0, row0);
+            bulk_commit_group();
+          }
+          bi ^= 1;
+        }
+      }
+      if (failed) break;
+    }
+    // every store of this warp completed before the CTA may exit
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
   } else {
     // --------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access

@@ -95,7 +95,7 @@ class FusedComm(CollectiveComm):
         self.fused_params = self.param_mode == "shard"
         src = getattr(config, "shard_source", "shadow")
         self.shard_source = src if src in ("master", "shadow") else "shadow"
-        self.gather_ctas = int(getattr(config, "shard_gather_ctas", 32))
+        self.gather_ctas = int(getattr(config, "shard_gather_ctas", 64))
 
     def disable_fused(self, params: bool, grads: bool) -> None:
         """Fall back to the NCCL path for parameter gathers and/or gradient

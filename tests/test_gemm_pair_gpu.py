@@ -1,6 +1,8 @@
 """CTA-pair (cta_group::2) GEMM vs an fp32 PyTorch product, in all three
 operand layouts and with the residual epilogue, at shapes with ragged M, N
-and K edges; also checks that the pair path leaves no error code."""
+and K edges, with both epilogues (register stores: mode 1; shared-memory
+staging + TMA stores: mode 2); also checks that the pair path leaves no
+error code."""
 import pytest
 import torch
 
@@ -16,11 +18,11 @@ def _rel(a, b):
     return ((a.float() - b).norm() / b.norm().clamp_min(1e-6)).item()
 
 
-@pytest.fixture
-def pair_mode():
+@pytest.fixture(params=[1, 2], ids=["regstore", "tmastore"])
+def pair_mode(request):
     C = _native.cuda()
     old = C.gemm_get_mode()
-    C.gemm_set_mode(1)
+    C.gemm_set_mode(request.param)
     C.gemm_check_error(True)
     yield C
     torch.cuda.synchronize()
@@ -63,3 +65,15 @@ def test_pair_wgrad(pair_mode, M, N, K):
     out = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
     native.linear_wgrad(dy, x, out=out)
     assert _rel(out, dy.float().t() @ x.float()) < 6e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 264, 200), (1000, 776, 1536)])
+def test_pair_wgrad_accumulate(pair_mode, M, N, K):
+    """wgrad with the residual epilogue on its own output (C += dy^T x)."""
+    g = torch.Generator(device="cuda").manual_seed(11)
+    dy = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    out = (torch.randn(N, K, device="cuda", generator=g) * 4).bfloat16()
+    expect = out.float() + dy.float().t() @ x.float()
+    native.gemm(dy, x, out, True, True, out)
+    assert _rel(out, expect) < 6e-3

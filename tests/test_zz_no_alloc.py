@@ -44,6 +44,12 @@ def _call(fn, dy, x, w, rstd, resid, dx, dw, T=None):
               T, H, stream)
 
 
+def _rows(t, T):
+    """View of the first T rows; the full buffer is what the C call gets, so
+    its pointers stay valid (non-null) when T is 0."""
+    return t[:T]
+
+
 @pytest.mark.parametrize("T,H", [(1024, 4096), (77, 8192), (5, 256), (33, 5120), (0, 1024)])
 def test_noalloc_matches_regular_binding(T, H, cuda_device):
     from test1_b200.ops import native
@@ -53,25 +59,30 @@ def test_noalloc_matches_regular_binding(T, H, cuda_device):
     g = torch.Generator(device="cuda").manual_seed(T + H)
     rows = max(T, 1)  # T = 0 still passes valid (unread) row buffers
     for call in range(2):  # the shared scratch keeps the previous call's contents
-        x = (torch.randn(rows, H, device="cuda", generator=g) * (call + 1)).bfloat16()[:T]
+        xb = (torch.randn(rows, H, device="cuda", generator=g) * (call + 1)).bfloat16()
         w = (torch.rand(H, device="cuda", generator=g) + 0.5).bfloat16()
-        dy = torch.randn(rows, H, device="cuda", generator=g).bfloat16()[:T]
-        resid = torch.randn(rows, H, device="cuda", generator=g).bfloat16()[:T] if call == 0 else None
+        dyb = torch.randn(rows, H, device="cuda", generator=g).bfloat16()
+        rb = torch.randn(rows, H, device="cuda", generator=g).bfloat16() if call == 0 else None
+        x, dy = _rows(xb, T), _rows(dyb, T)
+        resid = _rows(rb, T) if rb is not None else None
         if T:
             _, rstd = native.rmsnorm_fwd(x, w, 1e-5)
             dx_ref, dw_ref = native.rmsnorm_bwd(dy, x, w, rstd, resid)
+            rstdb = rstd
         else:
-            rstd = torch.zeros(1, device="cuda")[:0]
+            rstdb = torch.zeros(1, device="cuda")
+            rstd = rstdb[:0]
             dx_ref, dw_ref = torch.empty_like(x), torch.zeros_like(w)
         # fp32 oracle of the same formula
         dx32, dw32 = ref.rmsnorm_bwd(dy.float(), x.float(), w.float(), rstd,
                                      resid.float() if resid is not None else None)
-        dx = torch.empty(rows, H, device="cuda", dtype=torch.bfloat16)[:T]
+        dxb = torch.empty(rows, H, device="cuda", dtype=torch.bfloat16)
+        dx = _rows(dxb, T)
         dw = torch.full_like(w, float("nan"))  # must be overwritten, also for T = 0
         torch.cuda.synchronize()
         before = torch.cuda.memory_stats().get("allocation.all.allocated", 0)
         free_before = torch.cuda.mem_get_info()[0]
-        rc = _call(fn, dy, x, w, rstd, resid, dx, dw, T)
+        rc = _call(fn, dyb, xb, w, rstdb, rb, dxb, dw, T)
         torch.cuda.synchronize()
         free_after = torch.cuda.mem_get_info()[0]
         after = torch.cuda.memory_stats().get("allocation.all.allocated", 0)
