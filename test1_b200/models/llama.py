@@ -224,7 +224,26 @@ def _fused_rows(tensors: List[torch.Tensor]) -> torch.Tensor:
     return torch.cat(tensors, 0)
 
 
+def _wgrad_in_chunks(dy: torch.Tensor, x: torch.Tensor, out: torch.Tensor, ready, chunks: int) -> None:
+    """out = dy^T x, computed in ``chunks`` row blocks of ``out`` (256-row
+    aligned); ``ready`` gets each block as soon as it is final, so its
+    reduce-scatter and host store (on the gradient stream) overlap the
+    GEMM of the next block."""
+    rows = out.shape[0]
+    step = -(-rows // max(1, chunks))
+    step = -(-step // 256) * 256
+    for r0 in range(0, rows, step):
+        r1 = min(rows, r0 + step)
+        ops.linear_wgrad(dy[:, r0:r1], x, out=out[r0:r1])
+        ready(out[r0:r1])
+
+
 class LlamaDecoderLayer(nn.Module):
+    # row blocks of the two largest weight gradients when the engine syncs
+    # gradients per range (each block's reduce-scatter overlaps the next)
+    WGRAD_CHUNKS_GATE_UP = 4
+    WGRAD_CHUNKS_DOWN = 2
+
     def __init__(self, cfg: LlamaConfig, device=None, dtype=None):
         super().__init__()
         self.cfg = cfg
@@ -287,7 +306,8 @@ class LlamaDecoderLayer(nn.Module):
 
     def backward(self, saved, dh3: torch.Tensor, ctx: StepContext, grad_ready=None) -> torch.Tensor:
         """``grad_ready(t)``, when given, is called (on the compute stream's
-        timeline) with each weight gradient as soon as it is final: down,
+        timeline) with each weight gradient -- or, for the down and gate/up
+        projections, each row block of it -- as soon as it is final: down,
         gate/up, o, qkv; the norm gradients come last."""
         cfg = self.cfg
         ready = grad_ready if grad_ready is not None else (lambda t: None)
@@ -296,13 +316,17 @@ class LlamaDecoderLayer(nn.Module):
         w_qkv, w_o, w_gu, w_down = self._w()
         g_qkv, g_o, g_gu, g_down, g_ln1, g_ln2 = self._g()
         da = ops.linear_dgrad(dh3, w_down)
-        ops.linear_wgrad(dh3, a, out=g_down)
-        ready(g_down)
+        if grad_ready is not None:
+            _wgrad_in_chunks(dh3, a, g_down, ready, self.WGRAD_CHUNKS_DOWN)
+        else:
+            ops.linear_wgrad(dh3, a, out=g_down)
         dgu = ops.swiglu_bwd(da, gu)
         del da
         dx2 = ops.linear_dgrad(dgu, w_gu)
-        ops.linear_wgrad(dgu, x2, out=g_gu)
-        ready(g_gu)
+        if grad_ready is not None:
+            _wgrad_in_chunks(dgu, x2, g_gu, ready, self.WGRAD_CHUNKS_GATE_UP)
+        else:
+            ops.linear_wgrad(dgu, x2, out=g_gu)
         del dgu
         dh2, dw2 = ops.rmsnorm_bwd(dx2, h2, self.post_attention_layernorm.weight.data, rstd2, dh3)
         g_ln2.copy_(dw2)

@@ -157,3 +157,18 @@ def test_reference_linear_cross_entropy_chunks_agree_with_full_logits():
     l_full, dl, n_full = ref.cross_entropy_fwd_bwd(x @ w.t(), t)
     assert n == n_full and abs(float(loss) - float(l_full)) < 1e-5
     assert torch.allclose(dx, dl @ w, atol=1e-6) and torch.allclose(dw, dl.t() @ x, atol=1e-6)
+
+
+def test_wgrad_in_row_blocks_matches_one_product():
+    import torch
+
+    from test1_b200.models.llama import _wgrad_in_chunks
+
+    g = torch.Generator().manual_seed(1)
+    dy = torch.randn(64, 1000, generator=g)
+    x = torch.randn(64, 48, generator=g)
+    out = torch.empty(1000, 48)
+    seen = []
+    _wgrad_in_chunks(dy, x, out, lambda t: seen.append((t.data_ptr() - out.data_ptr()) // 4 // 48), 3)
+    assert torch.allclose(out, dy.t() @ x, atol=1e-4)
+    assert seen == [0, 512]  # 256-row aligned blocks: [0, 512), [512, 1000)
