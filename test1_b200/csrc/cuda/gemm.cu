@@ -41,7 +41,7 @@
 namespace t1 {
 
 // GEMM mode when neither T1_GEMM_MODE nor T1_GEMM_PAIR is set.
-constexpr int kDefaultGemmMode = 1;
+constexpr int kDefaultGemmMode = 2;
 
 // ================================================================ host side
 T1_BOUNDS_READER(gemm)
