@@ -51,7 +51,10 @@ void fused_shard_gather(torch::Tensor ptrs, torch::Tensor sigs, int64_t rank, in
 void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Tensor out,
                   torch::Tensor ptrs, torch::Tensor sigs, torch::Tensor shards, int64_t rank,
                   int64_t world, torch::Tensor host_src, c10::optional<torch::Tensor> host_src_lo,
-                  int64_t epoch, torch::Tensor counters);
+                  int64_t epoch, torch::Tensor counters, c10::optional<torch::Tensor> rope_cos,
+                  c10::optional<torch::Tensor> rope_sin, int64_t rope_S, int64_t rope_cols);
+void gemm_bf16_rope(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tensor cos_t,
+                    torch::Tensor sin_t, int64_t S, int64_t rope_cols);
 void multi_tensor_adam(int64_t chunk_size, torch::Tensor noop_flag,
                        std::vector<std::vector<torch::Tensor>> tensor_lists, double lr, double beta1,
                        double beta2, double eps, int64_t step, int64_t mode, int64_t bias_correction,
@@ -137,7 +140,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("rank"), pybind11::arg("world"), pybind11::arg("offset"), pybind11::arg("n"),
         pybind11::arg("host_src"), pybind11::arg("host_src_lo"), pybind11::arg("epoch"),
         pybind11::arg("counter"), pybind11::arg("err"), pybind11::arg("max_ctas") = 0);
-  m.def("fused_ag_qkv", &t1::fused_ag_qkv);
+  m.def("fused_ag_qkv", &t1::fused_ag_qkv, pybind11::arg("x"), pybind11::arg("unit"),
+        pybind11::arg("n_rows"), pybind11::arg("out"), pybind11::arg("ptrs"), pybind11::arg("sigs"),
+        pybind11::arg("shards"), pybind11::arg("rank"), pybind11::arg("world"), pybind11::arg("host_src"),
+        pybind11::arg("host_src_lo"), pybind11::arg("epoch"), pybind11::arg("counters"),
+        pybind11::arg("rope_cos") = pybind11::none(), pybind11::arg("rope_sin") = pybind11::none(),
+        pybind11::arg("rope_S") = 1, pybind11::arg("rope_cols") = 0);
+  m.def("gemm_bf16_rope", &t1::gemm_bf16_rope,
+        "C = A B^T with RoPE on columns [0, rope_cols) in the epilogue (GEMM mode 2)");
   m.def("multi_tensor_adam", &t1::multi_tensor_adam,
         "Adam/AdamW update of lists [grads, params, exp_avgs, exp_avg_sqs] (one launch per 192 tensors)");
 }

@@ -31,7 +31,8 @@ int64_t gemm_get_mode();
 void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Tensor out,
                   torch::Tensor ptrs, torch::Tensor sigs, torch::Tensor shards, int64_t rank,
                   int64_t world, torch::Tensor host_src, c10::optional<torch::Tensor> host_src_lo,
-                  int64_t epoch, torch::Tensor counters) {
+                  int64_t epoch, torch::Tensor counters, c10::optional<torch::Tensor> rope_cos,
+                  c10::optional<torch::Tensor> rope_sin, int64_t rope_S, int64_t rope_cols) {
   T1_CHECK_INPUT(x, torch::kBFloat16);
   T1_CHECK_INPUT(unit, torch::kBFloat16);
   T1_CHECK_INPUT(out, torch::kBFloat16);
@@ -129,6 +130,24 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
   p.ldr = 0;
   p.k_blocks = (K + gemm::BK - 1) / gemm::BK;
   p.err = gemm_error_word().data_ptr<int>();
+  p.rope_cos = p.rope_sin = nullptr;
+  p.rope_S = 1;
+  p.rope_cols = 0;
+  // RoPE in the epilogue (TMA-store mode only; otherwise the caller rotates)
+  const bool rope = rope_cos.has_value() && rope_cos->defined() && rope_cols > 0;
+  if (rope) {
+    TORCH_CHECK(gemm_get_mode() == 2, "the fused RoPE epilogue needs GEMM mode 2");
+    TORCH_CHECK(rope_sin.has_value() && rope_sin->defined() && rope_cos->scalar_type() == torch::kFloat32 &&
+                    rope_cos->is_cuda() && rope_cos->is_contiguous() && rope_sin->is_contiguous() &&
+                    rope_cos->dim() == 2 && rope_cos->size(1) == 64 && rope_cos->size(0) >= rope_S &&
+                    rope_sin->sizes() == rope_cos->sizes() && rope_S > 0,
+                "rope tables must be contiguous fp32 [>= S, 64]");
+    TORCH_CHECK(rope_cols % 128 == 0 && rope_cols <= n_rows, "rope_cols must be whole heads");
+    p.rope_cos = rope_cos->data_ptr<float>();
+    p.rope_sin = rope_sin->data_ptr<float>();
+    p.rope_S = static_cast<int>(rope_S);
+    p.rope_cols = static_cast<int>(rope_cols);
+  }
   if (gemm_get_mode() >= 1) {
     // CTA pairs: 256 x 256 tiles, the B row blocks match the arrival flags
     p.tiles_m = (M + gemm::PAIR_BM - 1) / gemm::PAIR_BM;
@@ -138,7 +157,17 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
     CUtensorMap tb = make_map(unit.data_ptr(), K, n_rows, K, gemm::PAIR_HALF);
     // every CTA gathers, so the grid spans all SMs even when tiles are few
     const int clusters = num_sms() / 2;
-    if (gemm_get_mode() == 2) {
+    if (gemm_get_mode() == 2 && rope) {
+      CUtensorMap tc = make_map(out.data_ptr(), n_rows, M, out.stride(0), 32);
+      auto kern = gemm::gemm_pair_kernel<false, false, gemm::kStore, true, true, true>;
+      static bool rope_configured = false;
+      if (!rope_configured) {
+        T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           gemm::PAIR_SMEM_BYTES_TMA));
+        rope_configured = true;
+      }
+      kern<<<2 * clusters, 256, gemm::PAIR_SMEM_BYTES_TMA, stream()>>>(ta, tb, p, ag, tc, tc);
+    } else if (gemm_get_mode() == 2) {
       CUtensorMap tc = make_map(out.data_ptr(), n_rows, M, out.stride(0), 32);
       auto kern = gemm::gemm_pair_kernel<false, false, gemm::kStore, true, true>;
       static bool tma_configured = false;
@@ -162,6 +191,7 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
     count_launch();
     return;
   }
+  TORCH_CHECK(!rope, "the fused RoPE epilogue needs the CTA-pair GEMM");
   p.tiles_m = (M + gemm::BM - 1) / gemm::BM;
   p.tiles_n = (n_rows + gemm::BN - 1) / gemm::BN;
   p.num_tiles = p.tiles_m * p.tiles_n;

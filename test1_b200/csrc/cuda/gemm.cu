@@ -114,10 +114,10 @@ void gemm_set_mode(int64_t mode) {
 
 int64_t gemm_get_mode() { return gemm_mode(); }
 
-template <bool A_MN, bool B_MN, int EPI, bool TMA_EPI>
+template <bool A_MN, bool B_MN, int EPI, bool TMA_EPI, bool ROPE = false>
 static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p,
                         const CUtensorMap& tc, const CUtensorMap& tr) {
-  auto kern = gemm::gemm_pair_kernel<A_MN, B_MN, EPI, false, TMA_EPI>;
+  auto kern = gemm::gemm_pair_kernel<A_MN, B_MN, EPI, false, TMA_EPI, ROPE>;
   constexpr int smem = TMA_EPI ? gemm::PAIR_SMEM_BYTES_TMA : gemm::PAIR_SMEM_BYTES;
   static bool configured = false;
   if (!configured) {
@@ -193,6 +193,9 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, boo
   p.num_tiles = p.tiles_m * p.tiles_n;
   p.k_blocks = (K + gemm::BK - 1) / gemm::BK;
   p.err = gemm_error_word().data_ptr<int>();
+  p.rope_cos = p.rope_sin = nullptr;
+  p.rope_S = 1;
+  p.rope_cols = 0;
   const bool add = R.has_value() && R->defined();
   if (add) {
     T1_CHECK_INPUT(*R, torch::kBFloat16);
@@ -223,6 +226,53 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, boo
     TORCH_CHECK(!add, "residual epilogue is built for the forward and wgrad layouts");
     launch<true, false, gemm::kStore>(ta, tb, p, tc, tr);
   }
+}
+
+// C = A B^T with the rotary embedding applied to columns [0, rope_cols) in
+// the epilogue (the QKV projection: q and k heads of head_dim 128 first).
+// A [M, K] and B [N, K] K-major; cos/sin fp32 [>= S, 64]; row r has position
+// r % S.  Needs the TMA-store epilogue (GEMM mode 2).
+void gemm_bf16_rope(torch::Tensor A, torch::Tensor B, torch::Tensor C, torch::Tensor cos_t,
+                    torch::Tensor sin_t, int64_t S, int64_t rope_cols) {
+  TORCH_CHECK(gemm_mode() == 2, "the RoPE epilogue needs GEMM mode 2 (TMA-store epilogue)");
+  T1_CHECK_INPUT(A, torch::kBFloat16);
+  T1_CHECK_INPUT(B, torch::kBFloat16);
+  T1_CHECK_INPUT(C, torch::kBFloat16);
+  T1_CHECK_INPUT(cos_t, torch::kFloat32);
+  T1_CHECK_INPUT(sin_t, torch::kFloat32);
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1 &&
+                  C.stride(1) == 1, "row-major 2-D operands expected");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K && C.size(0) == M && C.size(1) == N, "shapes: A [M, K], B [N, K], C [M, N]");
+  TORCH_CHECK(N % 8 == 0 && C.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(C.data_ptr()) % 16 == 0,
+              "C must have 16-byte aligned rows");
+  TORCH_CHECK(S > 0 && cos_t.is_contiguous() && sin_t.is_contiguous() && cos_t.dim() == 2 &&
+                  cos_t.size(1) == 64 && cos_t.size(0) >= S && sin_t.sizes() == cos_t.sizes(),
+              "rope tables must be contiguous fp32 [>= S, 64] (head_dim 128)");
+  TORCH_CHECK(rope_cols >= 0 && rope_cols % 128 == 0 && rope_cols <= N, "rope_cols must be whole heads");
+  if (M == 0 || N == 0) return;
+  TORCH_CHECK(K > 0, "K must be positive");
+  CUtensorMap ta = make_map(A.data_ptr(), K, M, A.stride(0), gemm::PAIR_HALF);
+  CUtensorMap tb = make_map(B.data_ptr(), K, N, B.stride(0), gemm::PAIR_HALF);
+  CUtensorMap tc = make_map(C.data_ptr(), N, M, C.stride(0), 32);
+  gemm::Params p;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = reinterpret_cast<bf16*>(C.data_ptr());
+  p.ldc = C.stride(0);
+  p.R = nullptr;
+  p.ldr = 0;
+  p.tiles_m = (M + gemm::PAIR_BM - 1) / gemm::PAIR_BM;
+  p.tiles_n = (N + gemm::PAIR_BN - 1) / gemm::PAIR_BN;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  p.k_blocks = (K + gemm::BK - 1) / gemm::BK;
+  p.err = gemm_error_word().data_ptr<int>();
+  p.rope_cos = cos_t.data_ptr<float>();
+  p.rope_sin = sin_t.data_ptr<float>();
+  p.rope_S = static_cast<int>(S);
+  p.rope_cols = static_cast<int>(rope_cols);
+  launch_pair<false, false, gemm::kStore, true, true>(ta, tb, p, tc, tc);
 }
 
 int64_t gemm_check_error(bool reset) {

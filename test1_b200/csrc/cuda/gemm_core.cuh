@@ -35,6 +35,12 @@ struct Params {
   long ldr;
   int tiles_m, tiles_n, num_tiles, k_blocks;
   int* err;
+  // RoPE fused into the epilogue (pair kernel, TMA stores, head_dim 128):
+  // columns [0, rope_cols) are rotated by position (row % rope_S) with the
+  // fp32 tables rope_cos / rope_sin [rope_S, 64]
+  const float* rope_cos;
+  const float* rope_sin;
+  int rope_S, rope_cols;
 };
 
 // Fused all-gather (shard mode): extra parameters of the AG variant.

@@ -26,6 +26,10 @@
 //     issues one bulk tensor store, double-buffered against the next slab.
 //     The accumulator is handed back to the MMA warp as soon as its last
 //     TMEM load finished, before the stores complete.
+//   ROPE (with TMA stores): the QKV projection's epilogue rotates the q and
+//     k heads (head_dim 128, rotate-half pairs (j, j + 64), angle of row
+//     position % S) on the fp32 accumulator before the one bf16 rounding;
+//     it works a whole head (two slabs) at a time.
 #pragma once
 
 #include "gemm_core.cuh"
@@ -50,7 +54,7 @@ static_assert(PAIR_SMEM_BYTES_TMA <= 232448, "pair GEMM with TMA epilogue exceed
 // fused_ag_gemm.cu): two more warps per CTA copy this rank's host shard of
 // the layer into every peer's unit, and the producers wait for the B rows
 // of a tile to arrive before loading them.
-template <bool A_MN, bool B_MN, int EPI, bool AG = false, bool TMA_EPI = false>
+template <bool A_MN, bool B_MN, int EPI, bool AG = false, bool TMA_EPI = false, bool ROPE = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b, const Params p, const AgParams ag,
@@ -236,6 +240,71 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
       raster(tile, p.tiles_m, p.tiles_n, mb, nb);
       const int row0 = mb * PAIR_BM + static_cast<int>(crank) * PAIR_HALF + q * 32;
       bool failed = false;
+      if (ROPE) {
+        // one head (128 columns, two slabs) per step; both buffers are
+        // rewritten, so every earlier store must have read them
+#pragma unroll 1
+        for (int c = 0; c < PAIR_BN; c += 128) {
+          const int col0 = nb * PAIR_BN + c;
+          const bool live = col0 < p.N && row0 < p.M;
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+          uint32_t r[4][32];
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * PAIR_BN + c;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) tmem_ld_32x32b_x32(taddr + 32 * k, r[k]);
+          tmem_ld_wait();
+          if (c + 128 == PAIR_BN) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+          }
+          if (!live) continue;
+          if (col0 < p.rope_cols) {
+            const int row = min(row0 + lane, p.M - 1);
+            const int pos = row % p.rope_S;
+            const float4* cp = reinterpret_cast<const float4*>(p.rope_cos + static_cast<size_t>(pos) * 64);
+            const float4* sp = reinterpret_cast<const float4*>(p.rope_sin + static_cast<size_t>(pos) * 64);
+#pragma unroll
+            for (int j4 = 0; j4 < 16; ++j4) {
+              const float4 cv = __ldg(cp + j4), sv = __ldg(sp + j4);
+              const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+              const float ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                const int j = 4 * j4 + u;
+                const float x1 = __uint_as_float(r[j >> 5][j & 31]);
+                const float x2 = __uint_as_float(r[(j + 64) >> 5][(j + 64) & 31]);
+                r[j >> 5][j & 31] = __float_as_uint(x1 * cc[u] - x2 * ss[u]);
+                r[(j + 64) >> 5][(j + 64) & 31] = __float_as_uint(x2 * cc[u] + x1 * ss[u]);
+              }
+            }
+          }
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint8_t* buf = wbuf + hh * PAIR_EPI_BUF;
+            uint8_t* rowp = buf + lane * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint4 ov;
+              __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                oh[k] = __floats2bfloat162_rn(__uint_as_float(r[2 * hh + (j >> 2)][(j & 3) * 8 + 2 * k]),
+                                              __uint_as_float(r[2 * hh + (j >> 2)][(j & 3) * 8 + 2 * k + 1]));
+              *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) = ov;
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tma_c, wbuf, col0, row0);
+            if (col0 + 64 < p.N) tma_store_2d(&tma_c, wbuf + PAIR_EPI_BUF, col0 + 64, row0);
+            bulk_commit_group();
+          }
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < PAIR_BN; c += 64) {
         uint8_t* buf = wbuf + bi * PAIR_EPI_BUF;

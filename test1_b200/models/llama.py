@@ -277,8 +277,9 @@ class LlamaDecoderLayer(nn.Module):
     # forward ---------------------------------------------------------------
     def forward_train(self, h: torch.Tensor, ctx: StepContext, save: bool = True, qkv_fn=None,
                       ln1_weight=None):
-        """``qkv_fn(x1)``, when given, produces the QKV projection (the engine
-        passes the fused all-gather + QKV GEMM of shard mode); the other
+        """``qkv_fn(x1, rope)``, when given, produces the rotated QKV projection
+        (the engine passes the fused all-gather + QKV GEMM of shard mode;
+        ``rope`` = (cos, sin, seq_len, n_q, n_kv, head_dim)); the other
         weights are read after it returns.  The input norm runs before that
         gather, so it then takes its weight from ``ln1_weight`` (fetched on
         its own by the engine) instead of the not-yet-filled unit."""
@@ -286,12 +287,12 @@ class LlamaDecoderLayer(nn.Module):
         Hq, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         w_ln1 = ln1_weight if ln1_weight is not None else self.input_layernorm.weight.data
         x1, rstd1 = ops.rmsnorm_fwd(h, w_ln1, cfg.rms_norm_eps)
+        rope = (ctx.cos, ctx.sin, ctx.seq_len, Hq, Hkv, D)
         if qkv_fn is not None:
-            qkv = qkv_fn(x1)
+            qkv = qkv_fn(x1, rope)
         else:
-            qkv = ops.linear_fwd(x1, self._w()[0])
+            qkv = ops.linear_fwd_rope(x1, self._w()[0], *rope)
         w_qkv, w_o, w_gu, w_down = self._w()
-        ops.rope_qkv_(qkv, Hq, Hkv, D, ctx.cos, ctx.sin, ctx.seq_len)
         o, lse = ops.attention_fwd(qkv, Hq, Hkv, D, ctx.seq_len)
         h2 = ops.linear_fwd(o, w_o, residual=h)
         x2, rstd2 = ops.rmsnorm_fwd(h2, self.post_attention_layernorm.weight.data, cfg.rms_norm_eps)

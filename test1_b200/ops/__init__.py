@@ -43,6 +43,13 @@ def linear_fwd(x, w, residual=None):
     return _impl(x).linear_fwd(x, w, residual)
 
 
+def linear_fwd_rope(x, w, cos, sin, seq_len, n_q, n_kv, head_dim):
+    """QKV projection with the rotary embedding of the q and k heads applied:
+    x @ w^T, then rotate column blocks [0, (n_q + n_kv) head_dim) by position
+    t % seq_len (on the GPU fused into the GEMM epilogue when possible)."""
+    return _impl(x).linear_fwd_rope(x, w, cos, sin, seq_len, n_q, n_kv, head_dim)
+
+
 def linear_dgrad(dy, w):
     return _impl(dy).linear_dgrad(dy, w)
 

@@ -44,6 +44,20 @@ def linear_fwd(x, w, residual=None):
     return out
 
 
+def rope_fusable(head_dim) -> bool:
+    """The GEMM epilogue applies RoPE for head_dim 128 in GEMM mode 2."""
+    return head_dim == 128 and gemm_get_mode() == 2
+
+
+def linear_fwd_rope(x, w, cos, sin, seq_len, n_q, n_kv, head_dim):
+    out = torch.empty(x.shape[0], w.shape[0], dtype=x.dtype, device=x.device)
+    if rope_fusable(head_dim) and x.is_contiguous() and w.is_contiguous():
+        _c().gemm_bf16_rope(x, w, out, cos, sin, int(seq_len), int((n_q + n_kv) * head_dim))
+        return out
+    _c().gemm_bf16(x, w, out, False, False, None)
+    return rope_qkv_(out, n_q, n_kv, head_dim, cos, sin, seq_len)
+
+
 def linear_dgrad(dy, w):
     out = torch.empty(dy.shape[0], w.shape[1], dtype=dy.dtype, device=dy.device)
     _c().gemm_bf16(dy, w, out, False, True, None)

@@ -67,6 +67,12 @@ def linear_dgrad(dy: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return (dy.to(dt) @ w.to(dt)).to(dy.dtype)
 
 
+def linear_fwd_rope(x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, seq_len: int,
+                    n_q: int, n_kv: int, head_dim: int) -> torch.Tensor:
+    qkv = linear_fwd(x, w)
+    return rope_qkv_(qkv, n_q, n_kv, head_dim, cos, sin, seq_len)
+
+
 def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     dt = _mm_dtype(dy)
     g = dy.to(dt).t() @ x.to(dt)

@@ -235,11 +235,14 @@ class FusedComm(CollectiveComm):
             self._shard_tables[key] = t
         return t
 
-    def ag_qkv(self, st: LayerRuntimeState, x1: torch.Tensor, n_rows: int) -> torch.Tensor:
+    def ag_qkv(self, st: LayerRuntimeState, x1: torch.Tensor, n_rows: int, rope=None) -> torch.Tensor:
         """Gather layer ``st`` into every rank's unit and return x1 @ W_qkv^T
-        (one kernel, on the current stream).  Staged: the shard already sits
-        in this rank's unit (``fetch_host_leg``), so the kernel's gather warps
-        read it from local memory and only push it to the peers."""
+        (one kernel, on the current stream), with the rotary embedding of the
+        q and k heads applied when ``rope`` = (cos, sin, seq_len, n_q, n_kv,
+        head_dim) is given -- in the kernel's epilogue when it can, else by
+        the RoPE kernel after it.  Staged: the shard already sits in this
+        rank's unit (``fetch_host_leg``), so the kernel's gather warps read it
+        from local memory and only push it to the peers."""
         s, e = shard_bounds(st.numel, self.world, self.rank)
         b = self._buf(st.unit.param)
         if self.staged:
@@ -247,9 +250,17 @@ class FusedComm(CollectiveComm):
         else:
             src, lo = self._gather_src(st, s, e)
         out = torch.empty(x1.shape[0], n_rows, dtype=x1.dtype, device=x1.device)
+        from ..ops import native
+
+        fuse_rope = rope is not None and native.rope_fusable(rope[5])
+        cos, sin, S, n_rot = (None, None, 1, 0) if not fuse_rope else (rope[0], rope[1], rope[2],
+                                                                      (rope[3] + rope[4]) * rope[5])
         _native.cuda().fused_ag_qkv(x1, b.tensor, n_rows, out, b.ptrs, b.sigs,
                                     self.shard_table(st.numel), self.rank, self.world, src, lo,
-                                    b.next_epoch(), b.ag_counters)
+                                    b.next_epoch(), b.ag_counters, cos, sin, S, n_rot)
+        if rope is not None and not fuse_rope:
+            cos, sin, S, n_q, n_kv, D = rope
+            native.rope_qkv_(out, n_q, n_kv, D, cos, sin, S)
         return out
 
     def _gather_src(self, st: LayerRuntimeState, s: int, e: int):

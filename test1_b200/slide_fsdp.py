@@ -924,7 +924,7 @@ class SlideFSDP(nn.Module):
                 else:
                     self._acquire_unloaded(st)
                 st.gather_pending = False
-                qkv_fn = (lambda x1, st=st: self.comm.ag_qkv(st, x1, n_qkv))
+                qkv_fn = (lambda x1, rope, st=st: self.comm.ag_qkv(st, x1, n_qkv, rope))
                 ln1 = self._early_weight(st, "input_layernorm.weight")
             else:
                 self._wait_loaded(st)

@@ -77,3 +77,30 @@ def test_pair_wgrad_accumulate(pair_mode, M, N, K):
     expect = out.float() + dy.float().t() @ x.float()
     native.gemm(dy, x, out, True, True, out)
     assert _rel(out, expect) < 6e-3
+
+
+@pytest.mark.parametrize("T,S,n_q,n_kv,K", [(4096, 1024, 32, 8, 4096), (300, 100, 4, 2, 512)])
+def test_qkv_gemm_with_fused_rope(T, S, n_q, n_kv, K):
+    """QKV projection with the rotary embedding applied in the TMA-store
+    epilogue (fp32 accumulator rotated before the bf16 rounding) against the
+    fp32 product rotated by the reference formula; v columns untouched."""
+    from test1_b200.ops import reference as ref
+
+    C = _native.cuda()
+    old = C.gemm_get_mode()
+    C.gemm_set_mode(2)
+    try:
+        D = 128
+        g = torch.Generator(device="cuda").manual_seed(T + S)
+        x = torch.randn(T, K, device="cuda", generator=g).bfloat16()
+        w = (torch.randn((n_q + 2 * n_kv) * D, K, device="cuda", generator=g) * 0.05).bfloat16()
+        cos, sin = ref.rope_tables(D, S, 500000.0, None, device="cuda")
+        out = native.linear_fwd_rope(x, w, cos, sin, S, n_q, n_kv, D)
+        expect = ref.rope_qkv_(x.float() @ w.float().t(), n_q, n_kv, D, cos, sin, S)
+        assert _rel(out, expect) < 6e-3
+        v0 = (n_q + n_kv) * D
+        assert _rel(out[:, v0:], expect[:, v0:]) < 6e-3
+        torch.cuda.synchronize()
+        assert C.gemm_check_error(True) == 0
+    finally:
+        C.gemm_set_mode(old)
