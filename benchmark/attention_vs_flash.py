@@ -4,7 +4,9 @@ config.py:82) on the same GPU, inputs and layout.
 
     python benchmark/attention_vs_flash.py [--shapes 4x1024,2x4096] [--json out.json]
 
-Both read q, k and v from one fused [B*S, (Hq + 2 Hkv) * D] bf16 projection
+Also times every forward variant of this library (mode 1: one query tile
+per CTA; mode 2: two tiles per CTA with 0, 1 or 2 of every 8 exponentials on
+the FMA-pipe polynomial).  Both read q, k and v from one fused [B*S, (Hq + 2 Hkv) * D] bf16 projection
 output (flash-attn gets strided [B, S, H, D] views of it, which it accepts
 without a copy).  Timed with CUDA events after warm-up, 20 launches per
 figure; attention is compute-bound, so no L2 flush is inserted.  FLOPs:
@@ -94,6 +96,19 @@ def run_shape(B, S, Hq=32, Hkv=8, D=128):
                      "speedup_vs_flash_attn2": round(fa / ours, 3), "peak_ref": tag})
     rows.append({"check": "max_abs_diff vs flash-attn 2", "B": B, "S": S, "o": diff_o, "dq": diff_dq,
                  "dk": diff_dk, "dv": diff_dv})
+    # every forward variant of this library on the same inputs
+    old = native.attn_get_mode()
+    variants = [(1, None)] + ([(2, k) for k in (0, 1, 2)] if S % 256 == 0 else [])
+    for mode, poly in variants:
+        native.attn_set_mode(mode)
+        if poly is not None:
+            native.attn_fwd2_set_poly(poly)
+        ms = timeit(lambda: native.attention_qkv_fwd(qkv, Hq, Hkv, D, S))
+        rows.append({"kernel": "attention_fwd_variant", "B": B, "S": S, "mode": mode, "poly_of_8": poly,
+                     "ms": round(ms, 4), "tflops": round(fl_f / ms / 1e9, 1),
+                     "frac_peak": round(fl_f / ms / 1e9 / tf_peak, 3), "peak_ref": tag})
+    native.attn_fwd2_set_poly(1)
+    native.attn_set_mode(old)
     return rows
 
 

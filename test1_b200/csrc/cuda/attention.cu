@@ -484,23 +484,27 @@ static void check_qkv(const torch::Tensor& qkv, int64_t n_q, int64_t n_kv, int64
 
 std::vector<torch::Tensor> attention_fwd_tc(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                             int64_t S);
+std::vector<torch::Tensor> attention_fwd_tc2(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t S);
 void attention_bwd_tc_core(torch::Tensor dout, torch::Tensor qkv, torch::Tensor lse,
                            torch::Tensor delta, torch::Tensor dq_acc, torch::Tensor dqkv, int64_t n_q,
                            int64_t n_kv, int64_t S);
 
 // Implementation of forward and backward: 0 = mma.sync tiles (this file),
-// 1 = tcgen05 (attention_tc.cu, the default).  Per process: attn_set_mode()
-// or T1_ATTN_TC=0/1.
+// 1 = tcgen05 with one 128-row query tile per CTA (attention_tc.cu),
+// 2 = the two-tile tcgen05 forward (attention_fwd2.cu, the default; it falls
+// back to mode 1 when seq_len is not a multiple of 256) with the tcgen05
+// backward.  Per process: attn_set_mode() or T1_ATTN_TC=0/1/2.
 static int& attn_mode() {
   static int mode = [] {
     const char* e = std::getenv("T1_ATTN_TC");
-    return (e != nullptr && e[0] == '0') ? 0 : 1;  // tcgen05 unless T1_ATTN_TC=0
+    if (e != nullptr && (e[0] == '0' || e[0] == '1')) return e[0] - '0';
+    return 2;
   }();
   return mode;
 }
 
 void attn_set_mode(int64_t mode) {
-  TORCH_CHECK(mode == 0 || mode == 1, "attention mode must be 0 (mma.sync) or 1 (tcgen05)");
+  TORCH_CHECK(mode >= 0 && mode <= 2, "attention mode must be 0 (mma.sync), 1 or 2 (tcgen05)");
   attn_mode() = static_cast<int>(mode);
 }
 
@@ -508,7 +512,11 @@ int64_t attn_get_mode() { return attn_mode(); }
 
 std::vector<torch::Tensor> attention_fwd(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                          int64_t S) {
-  if (attn_mode() == 1) return attention_fwd_tc(qkv, n_q, n_kv, D, S);
+  if (attn_mode() == 2 && S % 256 == 0) {
+    check_qkv(qkv, n_q, n_kv, D, S);
+    return attention_fwd_tc2(qkv, n_q, n_kv, S);
+  }
+  if (attn_mode() >= 1) return attention_fwd_tc(qkv, n_q, n_kv, D, S);
   check_qkv(qkv, n_q, n_kv, D, S);
   const int64_t T = qkv.size(0), B = T / S;
   auto out = torch::empty({T, n_q * D}, qkv.options());
@@ -547,7 +555,7 @@ torch::Tensor attention_bwd(torch::Tensor dout, torch::Tensor qkv, torch::Tensor
         delta.data_ptr<float>(), T, n_q);
     check_launch("attention_bwd_delta");
   }
-  if (attn_mode() == 1) {
+  if (attn_mode() >= 1) {
     attention_bwd_tc_core(dout, qkv, lse, delta, dq_acc, dqkv, n_q, n_kv, S);
   } else {
     const int smem = 6 * attn::TILE_BYTES + 64 * 128 + 4 * 64 * 4;

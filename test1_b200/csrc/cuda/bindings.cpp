@@ -32,12 +32,16 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, boo
                c10::optional<torch::Tensor> R);
 int64_t gemm_check_error(bool reset);
 void gemm_set_mode(int64_t mode);
+void gemm_set_streamk(bool on);
 int64_t gemm_get_mode();
 std::vector<torch::Tensor> attention_fwd(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                          int64_t S);
 std::vector<torch::Tensor> attention_fwd_tc(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                             int64_t S);
 void attn_set_mode(int64_t mode);
+void attn_fwd2_set_poly(int64_t n);
+void attn_fwd2_set_debug(torch::Tensor buf);
+std::vector<torch::Tensor> attention_fwd_tc2(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t S);
 int64_t attn_get_mode();
 torch::Tensor attention_bwd(torch::Tensor dout, torch::Tensor qkv, torch::Tensor out,
                             torch::Tensor lse, int64_t n_q, int64_t n_kv, int64_t D, int64_t S);
@@ -63,6 +67,7 @@ void multi_tensor_adam(int64_t chunk_size, torch::Tensor noop_flag,
 // bounds-checked builds
 unsigned long long bounds_word_attention(bool);
 unsigned long long bounds_word_attention_tc(bool);
+unsigned long long bounds_word_attention_fwd2(bool);
 unsigned long long bounds_word_elementwise(bool);
 unsigned long long bounds_word_embed_ce(bool);
 unsigned long long bounds_word_fused_adam(bool);
@@ -80,6 +85,7 @@ static std::vector<std::tuple<std::string, int64_t, int64_t>> bounds_errors(bool
   static const std::pair<const char*, Reader> readers[] = {
       {"attention.cu", &t1::bounds_word_attention},
       {"attention_tc.cu", &t1::bounds_word_attention_tc},
+      {"attention_fwd2.cu", &t1::bounds_word_attention_fwd2},
       {"elementwise.cu", &t1::bounds_word_elementwise},
       {"embed_ce.cu", &t1::bounds_word_embed_ce},
       {"fused_adam.cu", &t1::bounds_word_fused_adam},
@@ -129,11 +135,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("a_mn"), pybind11::arg("b_mn"), pybind11::arg("R") = pybind11::none());
   m.def("gemm_check_error", &t1::gemm_check_error, pybind11::arg("reset") = false);
   m.def("gemm_set_mode", &t1::gemm_set_mode, "0: single-CTA tiles, 1: CTA-pair (cta_group::2) tiles");
+  m.def("gemm_set_streamk", &t1::gemm_set_streamk, "stream-K tail of the TMA-store pair GEMM on/off");
   m.def("gemm_get_mode", &t1::gemm_get_mode);
   m.def("attention_fwd", &t1::attention_fwd);
   m.def("attention_bwd", &t1::attention_bwd);
   m.def("attention_fwd_tc", &t1::attention_fwd_tc);
-  m.def("attn_set_mode", &t1::attn_set_mode, "0: mma.sync forward, 1: tcgen05 forward");
+  m.def("attn_set_mode", &t1::attn_set_mode,
+        "0: mma.sync, 1: tcgen05 (one query tile per CTA), 2: tcgen05 forward with two query tiles per CTA");
+  m.def("attn_fwd2_set_poly", &t1::attn_fwd2_set_poly);
+  m.def("attn_fwd2_set_debug", &t1::attn_fwd2_set_debug, "phase-stamp buffer of the two-tile forward (empty = off)");
+  m.def("attention_fwd_tc2", &t1::attention_fwd_tc2);
   m.def("attn_get_mode", &t1::attn_get_mode);
   m.def("fused_rs_d2h", &t1::fused_rs_d2h);
   m.def("fused_shard_gather", &t1::fused_shard_gather, pybind11::arg("ptrs"), pybind11::arg("sigs"),

@@ -114,6 +114,58 @@ void gemm_set_mode(int64_t mode) {
 
 int64_t gemm_get_mode() { return gemm_mode(); }
 
+// Stream-K tail of the TMA-store pair kernel: off by default, T1_GEMM_STREAMK=1
+// or gemm_set_streamk(true) turns it on.
+static bool& streamk_on() {
+  static bool on = [] {
+    const char* e = std::getenv("T1_GEMM_STREAMK");
+    return e != nullptr && e[0] == '1';
+  }();
+  return on;
+}
+
+void gemm_set_streamk(bool on) { streamk_on() = on; }
+
+// Partial-sum workspace and arrival counters of the stream-K tail, one per
+// (device, stream), so GEMMs on different streams never share one; grown on
+// demand (the counters are zeroed once and reset by the kernel after use).
+struct SkWorkspace {
+  torch::Tensor ws, flags;
+};
+
+static SkWorkspace& sk_workspace(size_t floats, int flag_ints) {
+  static std::unordered_map<uint64_t, SkWorkspace> all;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const cudaStream_t st = stream();
+  const uint64_t key = (static_cast<uint64_t>(dev) << 56) ^ reinterpret_cast<uint64_t>(st);
+  SkWorkspace& w = all[key];
+  const auto opts = torch::TensorOptions().device(torch::kCUDA, dev);
+  if (!w.ws.defined() || static_cast<size_t>(w.ws.numel()) < floats)
+    w.ws = torch::empty({static_cast<int64_t>(floats)}, opts.dtype(torch::kFloat32));
+  if (!w.flags.defined() || w.flags.numel() < flag_ints)
+    w.flags = torch::zeros({flag_ints}, opts.dtype(torch::kInt32));
+  return w;
+}
+
+// Splits the last, partial wave of tiles along K when a cluster is free for
+// each half: with C clusters and R = num_tiles % C tail tiles (2 R <= C),
+// each tail tile becomes two pieces of >= 8 k-blocks in the same wave.
+static void plan_streamk(gemm::Params& p, int clusters) {
+  p.sk_split = 1;
+  p.sk_tail0 = 0;
+  p.num_units = p.num_tiles;
+  if (!streamk_on()) return;
+  const int R = p.num_tiles % clusters;
+  if (R == 0 || 2 * R > clusters || p.k_blocks < 16) return;
+  p.sk_split = 2;
+  p.sk_tail0 = p.num_tiles - R;
+  p.num_units = p.sk_tail0 + 2 * R;
+  SkWorkspace& w = sk_workspace(static_cast<size_t>(R) * gemm::kSkPartFloats, R * 8);
+  p.sk_ws = w.ws.data_ptr<float>();
+  p.sk_flags = w.flags.data_ptr<int>();
+}
+
 template <bool A_MN, bool B_MN, int EPI, bool TMA_EPI, bool ROPE = false>
 static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Params& p,
                         const CUtensorMap& tc, const CUtensorMap& tr) {
@@ -124,7 +176,12 @@ static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, gemm::Para
     T1_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured = true;
   }
-  const int clusters = std::min(p.num_tiles, num_sms() / 2);
+  if (TMA_EPI) plan_streamk(p, num_sms() / 2);
+  else {
+    p.sk_split = 1;
+    p.num_units = p.num_tiles;
+  }
+  const int clusters = std::min(p.num_units, num_sms() / 2);
   gemm::AgParams none{};
   kern<<<2 * clusters, 192, smem, stream()>>>(ta, tb, p, none, tc, tr);
   check_launch("gemm_bf16 (pair)");

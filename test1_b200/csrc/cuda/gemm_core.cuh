@@ -41,7 +41,36 @@ struct Params {
   const float* rope_cos;
   const float* rope_sin;
   int rope_S, rope_cols;
+  // Stream-K tail (pair kernel with the TMA-store epilogue): the tiles from
+  // sk_tail0 on (the last, partial wave) are each split along K into two
+  // pieces run by different clusters; the first writes its fp32 partial
+  // accumulator to sk_ws and counts its arrival in sk_flags, the second
+  // loads it, adds it before its epilogue and resets the counter.
+  // sk_split == 1 (the default) leaves one work unit per tile.
+  int sk_split = 1;
+  int sk_tail0 = 0;
+  int num_units = 0;         // sk_tail0 + (num_tiles - sk_tail0) * sk_split
+  float* sk_ws = nullptr;    // [tail tile][cta 2][warp 4][slab 4][row 32][64] fp32
+  int* sk_flags = nullptr;   // [tail tile][cta 2][quarter 4], zero between launches
 };
+
+// Work unit u of the pair kernel: its tile, k-block range [kb0, kb1) and
+// stream-K piece (-1: the whole tile).
+__device__ __forceinline__ void unit_info(const Params& p, int u, int& tile, int& kb0, int& kb1,
+                                          int& piece) {
+  if (p.sk_split <= 1 || u < p.sk_tail0) {
+    tile = u;
+    kb0 = 0;
+    kb1 = p.k_blocks;
+    piece = -1;
+    return;
+  }
+  const int i = u - p.sk_tail0;
+  tile = p.sk_tail0 + i / p.sk_split;
+  piece = i % p.sk_split;
+  kb0 = piece * p.k_blocks / p.sk_split;
+  kb1 = (piece + 1) * p.k_blocks / p.sk_split;
+}
 
 // Fused all-gather (shard mode): extra parameters of the AG variant.
 constexpr int kAgMaxRanks = 8;

@@ -50,6 +50,46 @@ constexpr int PAIR_EPI_BYTES = 4 /*warps*/ * 2 * PAIR_EPI_BUF;  // 32 KB
 constexpr int PAIR_SMEM_BYTES_TMA = PAIR_SMEM_BYTES + PAIR_EPI_BYTES;
 static_assert(PAIR_SMEM_BYTES_TMA <= 232448, "pair GEMM with TMA epilogue exceeds 227 KB of shared memory");
 
+// ---- stream-K tail helpers (see Params::sk_split)
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until *flag reaches target (false after the wait limit).
+__device__ __forceinline__ bool sk_wait(const int* flag, int target) {
+  if (ld_acquire_gpu(flag) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (ld_acquire_gpu(flag) < target) {
+    __nanosleep(128);
+    if ((++n & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+
+// Adds the first piece's partial sums of accumulator columns [c, c + 32)
+// of row `lane` from the staged [slab][row][64] block (swizzled as written).
+__device__ __forceinline__ void sk_add32(uint32_t (&r)[32], const uint8_t* stage, int c, int lane) {
+  const float4* row = reinterpret_cast<const float4*>(stage + (c >> 6) * 8192 + lane * 256);
+  const int half = (c >> 5) & 1;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 v = row[(half * 8 + j) ^ (lane & 7)];
+    r[4 * j + 0] = __float_as_uint(__uint_as_float(r[4 * j + 0]) + v.x);
+    r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) + v.y);
+    r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) + v.z);
+    r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) + v.w);
+  }
+}
+
+constexpr size_t kSkPartFloats = 2 * PAIR_HALF * PAIR_BN;  // one split tile's partial (both CTAs)
+
 // AG = true: the shard-mode fused all-gather variant (see gemm_core.cuh and
 // fused_ag_gemm.cu): two more warps per CTA copy this rank's host shard of
 // the layer into every peer's unit, and the producers wait for the B rows
@@ -70,7 +110,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
   uint64_t* tfull = empty + PAIR_STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* rbar = tempty + 2;  // [4] residual loads of the TMA epilogue, one per warp
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rbar + 4);
+  uint64_t* skbar = rbar + 4;   // [4] stream-K partial loads, one per warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(skbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -89,7 +130,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 8);  // 4 epilogue warps x 2 CTAs
     }
-    for (int w = 0; w < 4; ++w) mbar_init(&rbar[w], 1);
+    for (int w = 0; w < 4; ++w) {
+      mbar_init(&rbar[w], 1);
+      mbar_init(&skbar[w], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -110,13 +154,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int num_units = p.sk_split > 1 ? p.num_units : p.num_tiles;
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = cluster; tile < p.num_tiles && !*abort_flag; tile += nclusters) {
+      for (int u = cluster; u < num_units && !*abort_flag; u += nclusters) {
+        int tile, kb0, kb1, piece;
+        unit_info(p, u, tile, kb0, kb1, piece);
         int mb, nb;
         raster(tile, p.tiles_m, p.tiles_n, mb, nb);
         const int row_a = mb * PAIR_BM + static_cast<int>(crank) * PAIR_HALF;
@@ -135,7 +182,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
           }
           asm volatile("fence.proxy.async.global;" ::: "memory");
         }
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             err.set(111);
             *abort_flag = 1;
@@ -172,7 +219,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
-      for (int tile = cluster; tile < p.num_tiles && !*abort_flag; tile += nclusters, ++local) {
+      for (int u = cluster; u < num_units && !*abort_flag; u += nclusters, ++local) {
+        int tile, kb0, kb1, piece;
+        unit_info(p, u, tile, kb0, kb1, piece);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) {
@@ -183,7 +232,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * PAIR_BN;
         bool ok = true;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase)) {
             err.set(113);
             *abort_flag = 1;
@@ -199,7 +248,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
                                      : smem_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + k * 2048, 8192, 1024)
                                      : smem_desc_sw128(b_addr + k * 32, 16, 1024);
-            mma_bf16_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            mma_bf16_pair(d_tmem, ad, bd, IDESC, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           mma_commit_pair(&empty[stage], 0x3);
           if (++stage == PAIR_STAGES) {
@@ -222,7 +271,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
     uint32_t rphase = 0;
     int bi = 0;
     int local = 0;
-    for (int tile = cluster; tile < p.num_tiles; tile += nclusters, ++local) {
+    for (int u = cluster; u < num_units; u += nclusters, ++local) {
+      int tile, kb0, kb1, piece;
+      unit_info(p, u, tile, kb0, kb1, piece);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       int ok = 0;
@@ -240,6 +291,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
       raster(tile, p.tiles_m, p.tiles_n, mb, nb);
       const int row0 = mb * PAIR_BM + static_cast<int>(crank) * PAIR_HALF + q * 32;
       bool failed = false;
+      // stream-K (split in two): the first piece writes its partial sums and
+      // is done; the last piece brings them into shared memory with one bulk
+      // copy per warp and adds them on the way (sk_stage != nullptr)
+      const bool sk_writer = piece == 0;
+      const uint8_t* sk_stage = nullptr;
+      if (piece >= 0) {
+        const int ti = tile - p.sk_tail0;
+        // this warp's 32 rows of the partial: [slab 4][row 32][64 floats], the
+        // 16-byte units of a row XOR-swizzled by the row (lane & 7)
+        float* wsw = p.sk_ws + (static_cast<size_t>(ti) * 2 + crank) * kSkPartFloats / 2 +
+                     static_cast<size_t>(q) * (32 * PAIR_BN);
+        int* flag = p.sk_flags + (ti * 2 + static_cast<int>(crank)) * 4 + q;
+        if (sk_writer) {
+#pragma unroll 1
+          for (int c = 0; c < PAIR_BN; c += 32) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * PAIR_BN + c, r);
+            tmem_ld_wait();
+            if (c + 32 == PAIR_BN) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+            }
+            float4* row = reinterpret_cast<float4*>(wsw + (c >> 6) * 2048 + lane * 64);
+            const int half = (c >> 5) & 1;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              __stcg(row + ((half * 8 + j) ^ (lane & 7)),
+                     make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                 __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+          }
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) red_release_gpu_add(flag, 1);
+          continue;
+        }
+        // the last piece is this cluster's last unit: the operand ring is
+        // idle (every MMA that read it completed), 32 KB of it per warp
+        uint8_t* stage_buf = sA + q * (32 * PAIR_BN * 4);
+        int okf = 0;
+        if (lane == 0) {
+          okf = sk_wait(flag, 1);
+          if (okf) {
+            *flag = 0;  // consumed; the next launch starts from zero
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            mbar_arrive_expect_tx(&skbar[q], 32 * PAIR_BN * 4);
+            bulk_load_1d(stage_buf, wsw, 32 * PAIR_BN * 4, &skbar[q]);
+            okf = mbar_wait(&skbar[q], 0);
+          }
+          if (!okf) {
+            err.set(117);
+            *abort_flag = 1;
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, okf, 0)) break;
+        sk_stage = stage_buf;
+      }
       if (ROPE) {
         // one head (128 columns, two slabs) per step; both buffers are
         // rewritten, so every earlier store must have read them
@@ -254,6 +362,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) tmem_ld_32x32b_x32(taddr + 32 * k, r[k]);
           tmem_ld_wait();
+          if (sk_stage != nullptr) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) sk_add32(r[k], sk_stage, c + 32 * k, lane);
+          }
           if (c + 128 == PAIR_BN) {
             tc_fence_before();
             __syncwarp();
@@ -322,6 +434,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
         tmem_ld_32x32b_x32(taddr, r0);
         tmem_ld_32x32b_x32(taddr + 32, r1);
         tmem_ld_wait();
+        if (sk_stage != nullptr) {
+          sk_add32(r0, sk_stage, c, lane);
+          sk_add32(r1, sk_stage, c + 32, lane);
+        }
         if (c + 64 == PAIR_BN) {
           // every TMEM read of this accumulator is done: hand it back now
           tc_fence_before();
@@ -385,7 +501,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
     const uint32_t leader_tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
     const uint32_t leader_tempty1 = mapa_shared(smem_u32(&tempty[1]), 0);
     int local = 0;
-    for (int tile = cluster; tile < p.num_tiles; tile += nclusters, ++local) {
+    for (int tile = cluster; tile < num_units; tile += nclusters, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       // one lane waits and the warp follows it, so the warp never diverges

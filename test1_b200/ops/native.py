@@ -76,6 +76,12 @@ def gemm(a, b, c, a_mn=False, b_mn=False, residual=None):
     return c
 
 
+def gemm_set_streamk(on: bool) -> None:
+    """Stream-K tail of the default (TMA-store) pair GEMM: the last partial
+    wave of tiles is split along K over otherwise idle clusters."""
+    _c().gemm_set_streamk(bool(on))
+
+
 def gemm_set_mode(mode: int) -> None:
     """0: single-CTA 128x256 tiles; 1: CTA-pair (cta_group::2) 256x256 tiles."""
     _c().gemm_set_mode(int(mode))
@@ -86,8 +92,21 @@ def gemm_get_mode() -> int:
 
 
 def attn_set_mode(mode: int) -> None:
-    """Attention forward: 0 = mma.sync tiles, 1 = tcgen05 (TMEM accumulators)."""
+    """Attention: 0 = mma.sync tiles, 1 = tcgen05 (TMEM accumulators, one
+    128-row query tile per CTA), 2 = tcgen05 forward with two query tiles per
+    CTA in ping-pong (the default; sequences not a multiple of 256 use 1)."""
     _c().attn_set_mode(int(mode))
+
+
+def attn_fwd2_set_poly(n: int) -> None:
+    """Two-tile forward: how many of every 8 exponentials run as a polynomial
+    on the FMA pipe instead of the MUFU unit (0, 1 or 2)."""
+    _c().attn_fwd2_set_poly(int(n))
+
+
+def attention_fwd_tc2(qkv, n_q, n_kv, seq_len):
+    """The two-tile tcgen05 forward directly (seq_len % 256 == 0)."""
+    return _c().attention_fwd_tc2(qkv, n_q, n_kv, seq_len)
 
 
 def attn_get_mode() -> int:

@@ -104,3 +104,42 @@ def test_qkv_gemm_with_fused_rope(T, S, n_q, n_kv, K):
         assert C.gemm_check_error(True) == 0
     finally:
         C.gemm_set_mode(old)
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (512, 512, 2048), (4096, 6144, 4096), (768, 4096, 14336)])
+def test_streamk_tail_matches_reference(M, N, K):
+    """TMA-store pair GEMM with the stream-K tail (last partial wave split
+    along K, partial sums added by the last piece) in the forward, dgrad and
+    accumulating wgrad layouts: against the fp32 product, against the same
+    GEMM without the split, and twice in a row (the arrival counters are
+    reset by the kernel)."""
+    C = _native.cuda()
+    old = C.gemm_get_mode()
+    C.gemm_set_mode(2)
+    C.gemm_check_error(True)
+    try:
+        g = torch.Generator(device="cuda").manual_seed(M + K)
+        x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+        w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+        dy = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+        ref_f = x.float() @ w.float().t()
+        outs = []
+        for sk in (True, False, True):
+            C.gemm_set_streamk(sk)
+            y = native.linear_fwd(x, w)
+            dx = native.linear_dgrad(dy, w)
+            acc = (torch.randn(N, K, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1)) * 4).bfloat16()
+            expect_acc = acc.float() + dy.float().t() @ x.float()
+            native.gemm(dy, x, acc, True, True, acc)
+            assert _rel(y, ref_f) < 6e-3
+            assert _rel(dx, dy.float() @ w.float()) < 6e-3
+            assert _rel(acc, expect_acc) < 6e-3
+            outs.append(y)
+        # split vs unsplit: same fp32 sums up to the order of addition
+        assert _rel(outs[0], outs[1].float()) < 4e-3
+        assert torch.equal(outs[0], outs[2])
+        torch.cuda.synchronize()
+        assert C.gemm_check_error(True) == 0
+    finally:
+        C.gemm_set_streamk(False)
+        C.gemm_set_mode(old)

@@ -144,9 +144,11 @@ def test_cross_entropy(T, V):
 
 
 @pytest.mark.parametrize("B,S,nq,nkv", [(2, 128, 4, 2), (1, 1024, 32, 8), (2, 256, 8, 8)])
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 def test_attention_fwd_bwd(B, S, nq, nkv, mode):
-    """Both implementations (0 = mma.sync, 1 = tcgen05) vs the fp32 statement."""
+    """Every implementation (0 = mma.sync, 1 = tcgen05 one tile per CTA,
+    2 = tcgen05 two tiles per CTA, falling back to 1 when S % 256 != 0) vs
+    the fp32 statement."""
     old = native.attn_get_mode()
     native.attn_set_mode(mode)
     try:
@@ -194,6 +196,33 @@ def test_attention_tcgen05_forward_matches_reference(B, S, hq, hkv):
     assert torch.allclose(lse, lsee, atol=2e-3, rtol=1e-3)
     assert _rel(o, o0) < 1e-2
     assert torch.allclose(lse, lse0, atol=2e-3, rtol=1e-3)
+
+
+@pytest.mark.parametrize("poly", [0, 1, 2])
+@pytest.mark.parametrize("B,S,hq,hkv", [(2, 1024, 4, 2), (1, 256, 2, 1), (1, 2048, 8, 2)])
+def test_attention_two_tile_forward(B, S, hq, hkv, poly):
+    """Two-tile tcgen05 forward (ping-pong softmax warps, 0/1/2 of every 8
+    exponentials on the FMA-pipe polynomial) vs the fp32 statement and the
+    one-tile tcgen05 forward."""
+    D = 128
+    torch.manual_seed(B * S + hq + poly)
+    qkv = (torch.randn(B * S, (hq + 2 * hkv) * D, device="cuda") * 0.5).bfloat16()
+    old = native.attn_get_mode()
+    try:
+        native.attn_fwd2_set_poly(poly)
+        o2, lse2 = native.attention_fwd_tc2(qkv, hq, hkv, S)
+        native.attn_set_mode(1)
+        o1, lse1 = native.attention_qkv_fwd(qkv, hq, hkv, D, S)
+    finally:
+        native.attn_fwd2_set_poly(1)
+        native.attn_set_mode(old)
+    torch.cuda.synchronize()
+    assert native.gemm_error() == 0
+    oe, lsee = ref.attention_qkv_fwd(qkv.float(), hq, hkv, D, S)
+    assert _rel(o2, oe) < 1e-2
+    assert torch.allclose(lse2, lsee, atol=2e-3, rtol=1e-3)
+    assert _rel(o2, o1) < 1e-2
+    assert torch.allclose(lse2, lse1, atol=2e-3, rtol=1e-3)
 
 
 @pytest.mark.parametrize("B,S,nq,nkv", [(2, 256, 4, 2), (1, 320, 8, 2), (2, 1024, 4, 1)])
