@@ -107,7 +107,7 @@ def run_shape(B, S, Hq=32, Hkv=8, D=128):
         rows.append({"kernel": "attention_fwd_variant", "B": B, "S": S, "mode": mode, "poly_of_8": poly,
                      "ms": round(ms, 4), "tflops": round(fl_f / ms / 1e9, 1),
                      "frac_peak": round(fl_f / ms / 1e9 / tf_peak, 3), "peak_ref": tag})
-    native.attn_fwd2_set_poly(1)
+    native.attn_fwd2_set_poly(0)
     native.attn_set_mode(old)
     return rows
 

@@ -12,21 +12,25 @@
 //
 // One CTA per (256-query block, head, sequence), heaviest blocks first;
 // 320 threads:
-//   warp 0      TMA producer: Q_A and Q_B once, then K_0, V_0, K_1, V_1, ...
-//               through a 3-slot ring of 32 KB tiles (no multicast)
+//   warp 0      TMA producer: Q_A and Q_B once, then K_0, K_1, V_0, K_2,
+//               V_1, ... through a 3-slot ring of 32 KB tiles (no multicast)
 //   warp 1      TMEM owner (S_A | S_B | O_A | O_B, 512 columns) and the
 //               single-thread MMA issuer, in the order
-//                 S_A(0) S_B(0) { PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) }
-//               so the scores of one tile are computed while the other
-//               tile's softmax runs
+//                 S_A(0) S_B(0) { S_A(j+1) S_B(j+1) PV_A(j) PV_B(j) }
+//               where S_t(j+1) starts as soon as tile t's softmax warps
+//               have read S_t(j) into registers, so the next scores are
+//               ready when a softmax finishes and the two tiles' softmax
+//               phases overlap each other and the MMAs
 //   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B: thread =
 //               query row = TMEM lane; scale, causal mask, running max/sum in
 //               base 2 with lazy rescaling of O, P (bf16) into 128B-swizzled
 //               shared memory for the P V MMA; final O / l and the LSE.
-// Exponentials: most on the MUFU unit (ex2.approx), POLY of every 8 on the
-// FMA pipe as 2^x = 2^round(x) * p(x - round(x)), p a cubic interpolating
-// 2^r at the four Chebyshev nodes of [-0.5, 0.5] (max relative error 1.0e-4,
-// far below the bf16 rounding of P), so the two pipes share the load.
+// Exponentials: on the MUFU unit (ex2.approx) by default; POLY (0-2) of
+// every 8 can run on the FMA pipe instead as 2^x = 2^round(x) * p(x -
+// round(x)), p a cubic interpolating 2^r at the four Chebyshev nodes of
+// [-0.5, 0.5] (max relative error 1.0e-4, far below the bf16 rounding of P).
+// Measured on B200 (B=4, S=1024 and B=2, S=4096): POLY 0 fastest, 1 within
+// 2 %, 2 slower by 15-20 % (the extra registers spill).
 // Every wait is bounded (sm100.cuh); a timeout writes the error word.
 #include "common.cuh"
 #include "sm100.cuh"
@@ -105,6 +109,19 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, w, 0) != 0;
 }
 
+// Ring order: K_0, then K_{j+1}, V_j for j = 0, 1, ... (V_{n-1} last), so
+// the next block's keys are resident before this block's values are done
+// with: position of K_j is 0 (j = 0) or 2j - 1, of V_j 2j + 2 (or 2n - 1 for
+// the last block).
+__device__ __forceinline__ int pos_k(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int pos_v(int j, int n) { return j + 1 < n ? 2 * j + 2 : 2 * n - 1; }
+__device__ __forceinline__ void ring_item(int i, int n, bool& is_v, int& blk) {
+  if (i == 0) { is_v = false; blk = 0; return; }
+  if (i == 2 * n - 1) { is_v = true; blk = n - 1; return; }
+  is_v = (i & 1) == 0;          // even positions >= 2 hold V_{i/2 - 1}
+  blk = is_v ? i / 2 - 1 : (i + 1) / 2;
+}
+
 template <int POLY>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tma_qkv, const Params p) {
@@ -121,7 +138,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* s_full = bars + 7;   // [2]  S_t(j) computed
   uint64_t* p_full = bars + 9;   // [2]  P_t(j) written (4 warps)
   uint64_t* p_empty = bars + 11; // [2]  P_t(j) V_j completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* s_empty = bars + 13; // [2]  S_t(j) read into registers (4 warps)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -149,6 +167,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_full[t], 4);
       mbar_init(&p_empty[t], 1);
+      mbar_init(&s_empty[t], 4);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -184,8 +203,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         uint8_t* dst = sR + slot * TILE;
-        const int col = (i & 1) ? vcol : kcol;
-        const int row = tok0 + (i >> 1) * BN;
+        bool is_v;
+        int blk;
+        ring_item(i, nB, is_v, blk);
+        const int col = is_v ? vcol : kcol;
+        const int row = tok0 + blk * BN;
         mbar_arrive_expect_tx(&r_full[slot], TILE);
         tma_load_2d(dst, &tma_qkv, &r_full[slot], col, row);
         tma_load_2d(dst + BOX, &tma_qkv, &r_full[slot], col + 64, row);
@@ -208,7 +230,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       };
       // S_t(j) = Q_t K_j^T
       auto issue_s = [&](int t, int j) {
-        const uint32_t k_addr = r_addr + ((2 * j) % RING) * TILE;
+        const uint32_t k_addr = r_addr + (pos_k(j) % RING) * TILE;
         const uint32_t qa = q_addr + t * TILE;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k)
@@ -220,7 +242,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!mbar_wait(&p_full[t], j & 1)) { err.set(303 + t); return false; }
         if (dbg != nullptr && j < 32) dbg[512 + 2 * j + t] = clock64();
         tc_fence_after();
-        const uint32_t v_addr = r_addr + ((2 * j + 1) % RING) * TILE;
+        const uint32_t v_addr = r_addr + (pos_v(j, nB) % RING) * TILE;
         const uint32_t pa = p_addr + t * TILE;
 #pragma unroll
         for (int k = 0; k < BN / 16; ++k) {
@@ -232,28 +254,31 @@ __global__ void __launch_bounds__(THREADS, 1)
       };
       bool ok = mbar_wait(q_full, 0);
       if (!ok) err.set(305);
-      if (ok) ok = item_ready(0);
+      if (ok) ok = item_ready(pos_k(0));
       if (ok) {
         issue_s(0, 0);
         issue_s(1, 0);
-        mma_commit(&r_empty[0]);  // K_0 read by both tiles
+        mma_commit(&r_empty[pos_k(0) % RING]);  // K_0 read by both tiles
       }
+      // per block j: the next scores of each tile as soon as its softmax
+      // warps have read the current ones, then P V of both tiles
       for (int j = 0; ok && j < nB && !*abort_flag; ++j) {
-        if (!item_ready(2 * j + 1)) { ok = false; break; }  // V_j
-        if (j < nA) {
-          if (!issue_pv(0, j)) { ok = false; break; }
+        if (j + 1 < nB) {
+          if (!item_ready(pos_k(j + 1))) { ok = false; break; }
           if (j + 1 < nA) {
-            if (!item_ready(2 * j + 2)) { ok = false; break; }
+            if (!mbar_wait(&s_empty[0], j & 1)) { err.set(312); ok = false; break; }
+            tc_fence_after();
             issue_s(0, j + 1);
           }
-        }
-        if (!issue_pv(1, j)) { ok = false; break; }
-        mma_commit(&r_empty[(2 * j + 1) % RING]);  // V_j read by both tiles
-        if (j + 1 < nB) {
-          if (!item_ready(2 * j + 2)) { ok = false; break; }
+          if (!mbar_wait(&s_empty[1], j & 1)) { err.set(313); ok = false; break; }
+          tc_fence_after();
           issue_s(1, j + 1);
-          mma_commit(&r_empty[(2 * j + 2) % RING]);  // K_{j+1} read by both tiles
+          mma_commit(&r_empty[pos_k(j + 1) % RING]);  // K_{j+1} read by both tiles
         }
+        if (!item_ready(pos_v(j, nB))) { ok = false; break; }
+        if (j < nA && !issue_pv(0, j)) { ok = false; break; }
+        if (!issue_pv(1, j)) { ok = false; break; }
+        mma_commit(&r_empty[pos_v(j, nB) % RING]);  // V_j read by both tiles
       }
       if (!ok) *abort_flag = 1;
     }
@@ -291,6 +316,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(u[c][i]);
       }
+      // S_t is free for the next block's scores
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[t]);
       stamp(j, 1);
       // causal mask: only the tile's diagonal block (and a block crossing
       // the sequence end) needs it
@@ -413,7 +442,7 @@ T1_BOUNDS_READER(attention_fwd2)
 static int& attn_poly() {
   static int v = [] {
     const char* e = std::getenv("T1_ATTN_POLY");
-    return (e != nullptr && e[0] >= '0' && e[0] <= '2') ? e[0] - '0' : 1;
+    return (e != nullptr && e[0] >= '0' && e[0] <= '2') ? e[0] - '0' : 0;
   }();
   return v;
 }
@@ -468,12 +497,12 @@ std::vector<torch::Tensor> attention_fwd_tc2(torch::Tensor qkv, int64_t n_q, int
   p.ld_out = out.stride(0);
   p.lse = lse.data_ptr<float>();
   p.err = gemm_error_word().data_ptr<int>();
-  p.dbg = attn_fwd2_debug().defined() ? attn_fwd2_debug().data_ptr<long long>() : nullptr;
+  p.dbg = attn_fwd2_debug().defined() ? reinterpret_cast<long long*>(attn_fwd2_debug().data_ptr<int64_t>()) : nullptr;
   dim3 grid(n_q, B, S / (2 * attn_tc2::BM));
   switch (attn_poly()) {
-    case 0: launch_fwd2<0>(map, p, grid); break;
+    case 1: launch_fwd2<1>(map, p, grid); break;
     case 2: launch_fwd2<2>(map, p, grid); break;
-    default: launch_fwd2<1>(map, p, grid); break;
+    default: launch_fwd2<0>(map, p, grid); break;
   }
   check_launch("attention_fwd_tc2");
   count_launch();

@@ -106,7 +106,7 @@ def test_qkv_gemm_with_fused_rope(T, S, n_q, n_kv, K):
         C.gemm_set_mode(old)
 
 
-@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (512, 512, 2048), (4096, 6144, 4096), (768, 4096, 14336)])
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 4096), (512, 512, 2048), (4096, 4096, 14336), (768, 4096, 14336)])
 def test_streamk_tail_matches_reference(M, N, K):
     """TMA-store pair GEMM with the stream-K tail (last partial wave split
     along K, partial sums added by the last piece) in the forward, dgrad and
@@ -141,5 +141,5 @@ def test_streamk_tail_matches_reference(M, N, K):
         torch.cuda.synchronize()
         assert C.gemm_check_error(True) == 0
     finally:
-        C.gemm_set_streamk(False)
+        C.gemm_set_streamk(True)
         C.gemm_set_mode(old)

@@ -214,7 +214,7 @@ def test_attention_two_tile_forward(B, S, hq, hkv, poly):
         native.attn_set_mode(1)
         o1, lse1 = native.attention_qkv_fwd(qkv, hq, hkv, D, S)
     finally:
-        native.attn_fwd2_set_poly(1)
+        native.attn_fwd2_set_poly(0)
         native.attn_set_mode(old)
     torch.cuda.synchronize()
     assert native.gemm_error() == 0
