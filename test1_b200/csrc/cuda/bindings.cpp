@@ -33,6 +33,7 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor C, bool a_mn, boo
 int64_t gemm_check_error(bool reset);
 void gemm_set_mode(int64_t mode);
 void gemm_set_streamk(bool on);
+void fused_set_peer_wait(double seconds);
 int64_t gemm_get_mode();
 std::vector<torch::Tensor> attention_fwd(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                          int64_t S);
@@ -135,6 +136,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("a_mn"), pybind11::arg("b_mn"), pybind11::arg("R") = pybind11::none());
   m.def("gemm_check_error", &t1::gemm_check_error, pybind11::arg("reset") = false);
   m.def("gemm_set_mode", &t1::gemm_set_mode, "0: single-CTA tiles, 1: CTA-pair (cta_group::2) tiles");
+  m.def("fused_set_peer_wait", &t1::fused_set_peer_wait,
+        "limit (seconds) of the fused NVLink kernels' waits on peer GPUs (default 60)");
   m.def("gemm_set_streamk", &t1::gemm_set_streamk, "stream-K tail of the TMA-store pair GEMM on/off");
   m.def("gemm_get_mode", &t1::gemm_get_mode);
   m.def("attention_fwd", &t1::attention_fwd);

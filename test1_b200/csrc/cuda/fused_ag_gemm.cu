@@ -20,6 +20,8 @@
 
 namespace t1 {
 
+uint64_t fused_peer_wait_ns();
+
 T1_BOUNDS_READER(fused_ag_gemm)
 
 CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer);
@@ -107,6 +109,7 @@ void fused_ag_qkv(torch::Tensor x, torch::Tensor unit, int64_t n_rows, torch::Te
     ag.src_kind = host_src.scalar_type() == torch::kFloat32 ? 1 : 0;
   }
   ag.epoch = static_cast<uint32_t>(epoch);
+  ag.wait_ns = fused_peer_wait_ns();
   ag.n_blocks = static_cast<int>(n_blocks);
   ag.block_elems = static_cast<long>(gemm::BN) * K;
   // owners of each 256-row block: ranks whose shard intersects its elements

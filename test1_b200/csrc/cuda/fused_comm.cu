@@ -37,6 +37,7 @@ constexpr int kMaxRanks = 8;
 struct Peers {
   uint64_t ptr[kMaxRanks];  // base address of the symmetric buffer on each rank
   uint64_t sig[kMaxRanks];  // signal pad base on each rank
+  uint64_t wait_ns;         // limit of every wait on a peer
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -50,12 +51,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Wait until pad[slot0 + p] >= epoch for every p < world.  Thread-local.
-__device__ __forceinline__ bool wait_all(const uint32_t* pad, int slot0, int world, uint32_t epoch) {
+__device__ __forceinline__ bool wait_all(const uint32_t* pad, int slot0, int world, uint32_t epoch,
+                                         uint64_t wait_ns) {
   const uint64_t t0 = sm100::globaltimer_ns();
   for (int p = 0; p < world; ++p) {
     uint32_t n = 0;
     while (ld_acquire_sys(pad + slot0 + p) < epoch) {
-      if ((++n & 255u) == 0 && sm100::globaltimer_ns() - t0 > sm100::kWaitLimitNs) return false;
+      if ((++n & 255u) == 0 && sm100::globaltimer_ns() - t0 > wait_ns) return false;
     }
   }
   return true;
@@ -69,10 +71,10 @@ __device__ __forceinline__ void signal_all(const Peers& pe, int slot, int world,
 // Block-wide "all peers reached slot0 phase" barrier entry; returns false
 // (for every thread) when the wait expired.
 __device__ __forceinline__ bool block_wait(const uint32_t* my_pad, int slot0, int world,
-                                           uint32_t epoch, int* err, int code) {
+                                           uint32_t epoch, uint64_t wait_ns, int* err, int code) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
-    ok = wait_all(my_pad, slot0, world, epoch) ? 1 : 0;
+    ok = wait_all(my_pad, slot0, world, epoch, wait_ns) ? 1 : 0;
     if (!ok && err) atomicCAS(err, 0, code);
     __threadfence_system();
   }
@@ -91,7 +93,7 @@ __device__ __forceinline__ void finish(const Peers& pe, int rank, int world, uin
     if (prev == static_cast<int>(gridDim.x) - 1) {
       signal_all(pe, world + rank, world, epoch);
       const uint32_t* my_pad = reinterpret_cast<const uint32_t*>(pe.sig[rank]);
-      if (!wait_all(my_pad, world, world, epoch) && err) atomicCAS(err, 0, code);
+      if (!wait_all(my_pad, world, world, epoch, pe.wait_ns) && err) atomicCAS(err, 0, code);
       atomicExch(counter, 0);
     }
   }
@@ -104,7 +106,7 @@ __global__ void __launch_bounds__(256) rs_d2h_kernel(Peers pe, int rank, int wor
                                                      int* err) {
   if (blockIdx.x == 0 && threadIdx.x == 0) signal_all(pe, rank, world, epoch);  // my grads ready
   const uint32_t* my_pad = reinterpret_cast<const uint32_t*>(pe.sig[rank]);
-  if (!block_wait(my_pad, 0, world, epoch, err, 201)) return;
+  if (!block_wait(my_pad, 0, world, epoch, pe.wait_ns, err, 201)) return;
   const long n8 = n >> 3;
   const long stride = static_cast<long>(gridDim.x) * blockDim.x;
   for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += stride) {
@@ -187,7 +189,7 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, i
   // my unit is free (stream order): announce it, wait until every peer's is
   if (blockIdx.x == 0 && threadIdx.x == 0) signal_all(pe, rank, world, epoch);
   const uint32_t* my_pad = reinterpret_cast<const uint32_t*>(pe.sig[rank]);
-  if (!block_wait(my_pad, 0, world, epoch, err, 211)) return;
+  if (!block_wait(my_pad, 0, world, epoch, pe.wait_ns, err, 211)) return;
   const long n8 = n >> 3;
   const long stride = static_cast<long>(gridDim.x) * blockDim.x;
   // kU vectors per thread in flight: the loads (local HBM or PCIe) are
@@ -223,6 +225,24 @@ __global__ void __launch_bounds__(256) shard_gather_kernel(Peers pe, int rank, i
 // ================================================================ host side
 T1_BOUNDS_READER(fused_comm)
 
+// Limit of the fused kernels' waits on peer GPUs (T1_PEER_WAIT_S or
+// fused_set_peer_wait; default 60 s).
+static uint64_t& peer_wait_ns() {
+  static uint64_t v = [] {
+    const char* e = std::getenv("T1_PEER_WAIT_S");
+    const double s = e != nullptr ? std::atof(e) : 0.0;
+    return s > 0.0 ? static_cast<uint64_t>(s * 1e9) : sm100::kPeerWaitDefaultNs;
+  }();
+  return v;
+}
+
+void fused_set_peer_wait(double seconds) {
+  TORCH_CHECK(seconds > 0.0 && seconds <= 3600.0, "peer wait limit must be in (0, 3600] seconds");
+  peer_wait_ns() = static_cast<uint64_t>(seconds * 1e9);
+}
+
+uint64_t fused_peer_wait_ns() { return peer_wait_ns(); }
+
 static fused::Peers make_peers(torch::Tensor ptrs, torch::Tensor sigs, int world) {
   TORCH_CHECK(world >= 1 && world <= fused::kMaxRanks, "world size must be 1..8");
   TORCH_CHECK(ptrs.device().is_cpu() && ptrs.scalar_type() == torch::kInt64 && ptrs.numel() == world,
@@ -237,6 +257,7 @@ static fused::Peers make_peers(torch::Tensor ptrs, torch::Tensor sigs, int world
     pe.sig[i] = i < world ? static_cast<uint64_t>(sa[i]) : 0;
     if (i < world) TORCH_CHECK(pe.ptr[i] % 16 == 0, "peer buffer ", i, " is not 16-byte aligned");
   }
+  pe.wait_ns = peer_wait_ns();
   return pe;
 }
 

@@ -90,6 +90,7 @@ struct AgParams {
   long block_elems;            // 256 * K
   uint8_t owners[kAgMaxBlocks];  // bitmask of ranks whose shard intersects block b
   int* counters;               // kAgMaxBlocks + 1 device ints, zero between launches
+  uint64_t wait_ns;            // limit of every wait on a peer
 };
 
 __device__ __forceinline__ void raster(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
@@ -112,11 +113,11 @@ __device__ __forceinline__ uint32_t ag_load_acquire(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ bool ag_wait_geq(const uint32_t* p, uint32_t epoch) {
+__device__ __forceinline__ bool ag_wait_geq(const uint32_t* p, uint32_t epoch, uint64_t wait_ns) {
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
   while (ag_load_acquire(p) < epoch) {
-    if ((++n & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if ((++n & 255u) == 0 && globaltimer_ns() - t0 > wait_ns) return false;
   }
   return true;
 }
@@ -202,7 +203,7 @@ __device__ __forceinline__ void ag_gather_warps(const AgParams& ag, const ErrorS
     __shared__ int ag_ok;
     if (gt == 0) {
       bool ok = true;
-      for (int q = 0; q < ag.world && ok; ++q) ok = ag_wait_geq(pad + q, ag.epoch);
+      for (int q = 0; q < ag.world && ok; ++q) ok = ag_wait_geq(pad + q, ag.epoch, ag.wait_ns);
       ag_ok = ok;
       if (!ok) {
         err.set(122);
@@ -255,7 +256,7 @@ __device__ __forceinline__ void ag_gather_warps(const AgParams& ag, const ErrorS
         // last CTA: everything this rank owns is out; wait for every peer's
         ag_signal_all(ag, ag.world + ag.rank);
         bool ok = true;
-        for (int q = 0; q < ag.world && ok; ++q) ok = ag_wait_geq(pad + ag.world + q, ag.epoch);
+        for (int q = 0; q < ag.world && ok; ++q) ok = ag_wait_geq(pad + ag.world + q, ag.epoch, ag.wait_ns);
         if (!ok) err.set(123);
         atomicExch(&ag.counters[kAgMaxBlocks], 0);
       }
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(AG ? 256 : 192, 1)
           bool ok = true;
           for (int q = 0; q < ag.world && ok; ++q)
             if (ag.owners[nb] & (1u << q))
-              ok = ag_wait_geq(pad + 2 * ag.world + nb * ag.world + q, ag.epoch);
+              ok = ag_wait_geq(pad + 2 * ag.world + nb * ag.world + q, ag.epoch, ag.wait_ns);
           if (!ok) {
             err.set(121);
             *abort_flag = 1;

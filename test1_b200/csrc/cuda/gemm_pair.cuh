@@ -174,7 +174,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(AG ? 256 : 192, 1)
           bool ok = true;
           for (int q = 0; q < ag.world && ok; ++q)
             if (ag.owners[nb] & (1u << q))
-              ok = ag_wait_geq(pad + 2 * ag.world + nb * ag.world + q, ag.epoch);
+              ok = ag_wait_geq(pad + 2 * ag.world + nb * ag.world + q, ag.epoch, ag.wait_ns);
           if (!ok) {
             err.set(115);
             *abort_flag = 1;

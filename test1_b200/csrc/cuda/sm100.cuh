@@ -23,6 +23,11 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s: no legitimate wait is this long
+// Waits on another GPU's progress (the fused NVLink kernels) get a longer
+// default limit, set per launch from the host (fused_set_peer_wait): ranks
+// can legitimately drift apart by seconds (a host stall, a rank's first-step
+// set-up), and a peer wait that expires aborts the collective on every rank.
+constexpr uint64_t kPeerWaitDefaultNs = 60000000000ull;  // 60 s
 
 // Error word written when a bounded wait expires (host reads it back).
 struct ErrorSlot {

@@ -96,6 +96,7 @@ class FusedComm(CollectiveComm):
         src = getattr(config, "shard_source", "shadow")
         self.shard_source = src if src in ("master", "shadow") else "shadow"
         self.gather_ctas = int(getattr(config, "shard_gather_ctas", 64))
+        self._peer_tail = None  # completion event of the last peer-waiting kernel
 
     def disable_fused(self, params: bool, grads: bool) -> None:
         """Fall back to the NCCL path for parameter gathers and/or gradient
@@ -131,6 +132,38 @@ class FusedComm(CollectiveComm):
         # the fused reduce-scatter already multiplies by 1/N
         return 1.0 if self.fused_grads else 1.0 / self.world
 
+    # ordering of the kernels that wait on peer GPUs ----------------------
+    def _peer_launch(self, stream: Optional[torch.cuda.Stream] = None):
+        """Context for one launch of a kernel that waits on peer GPUs (a
+        gather, a reduce-scatter or the fused QKV GEMM): it starts only after
+        the previous such kernel of this rank completed, on whatever stream.
+        Every rank launches them in the same program order, so each GPU then
+        runs them in that order and the k-th kernel of one rank always meets
+        the k-th of the others.  Without it, two of them on different streams
+        can start in different orders on two GPUs; one that holds every SM
+        (the fused QKV GEMM) keeps the other from starting, and each rank
+        waits for a peer kernel that cannot run (seen as expired peer waits,
+        errors 211/212, in a 2-GPU shard-mode run)."""
+        fc = self
+
+        class _Ctx:
+            def __enter__(self_):
+                s = stream if stream is not None else torch.cuda.current_stream(fc.device)
+                self_.s = s
+                self_.cm = torch.cuda.stream(s)
+                self_.cm.__enter__()
+                if fc._peer_tail is not None:
+                    s.wait_event(fc._peer_tail)
+                return s
+
+            def __exit__(self_, *exc):
+                ev = torch.cuda.Event()
+                ev.record(self_.s)
+                fc._peer_tail = ev
+                return self_.cm.__exit__(*exc)
+
+        return _Ctx()
+
     # operations ----------------------------------------------------------
     @property
     def staged(self) -> bool:
@@ -157,13 +190,13 @@ class FusedComm(CollectiveComm):
         if self.fetch_host_leg(st, dst, stream):
             # NVLink leg on a few CTAs: the shard, now in this rank's unit,
             # into every peer's
-            with stream.ctx():
+            with self._peer_launch(stream.s):
                 _native.cuda().fused_shard_gather(b.ptrs, b.sigs, self.rank, self.world, s, e - s,
                                                   dst[s:e] if e > s else dst[:0], None, b.next_epoch(),
                                                   b.counter, self.err, self.gather_ctas)
             return
         src, lo = self._gather_src(st, s, e)
-        with stream.ctx():
+        with self._peer_launch(stream.s):
             _native.cuda().fused_shard_gather(b.ptrs, b.sigs, self.rank, self.world, s, e - s,
                                               src, lo, b.next_epoch(), b.counter, self.err)
 
@@ -193,7 +226,7 @@ class FusedComm(CollectiveComm):
         s, e = shard_bounds(st.numel, self.world, self.rank)
         b = self._buf(src)
         out = st.grad_host if st.grad_host is not None else torch.empty(0, dtype=src.dtype)
-        with stream.ctx():
+        with self._peer_launch(stream.s):
             _native.cuda().fused_rs_d2h(b.ptrs, b.sigs, self.rank, self.world, s, e - s, out,
                                         1.0 / self.world, b.next_epoch(), b.counter, self.err)
 
@@ -212,7 +245,7 @@ class FusedComm(CollectiveComm):
             out = st.grad_host[a - s: a - s + n]
         else:
             out, a, n = torch.empty(0, dtype=src.dtype), lo, 0
-        with stream.ctx():
+        with self._peer_launch(stream.s):
             _native.cuda().fused_rs_d2h(buf.ptrs, buf.sigs, self.rank, self.world, a, n, out,
                                         1.0 / self.world, buf.next_epoch(), buf.counter, self.err)
 
@@ -255,9 +288,10 @@ class FusedComm(CollectiveComm):
         fuse_rope = rope is not None and native.rope_fusable(rope[5])
         cos, sin, S, n_rot = (None, None, 1, 0) if not fuse_rope else (rope[0], rope[1], rope[2],
                                                                       (rope[3] + rope[4]) * rope[5])
-        _native.cuda().fused_ag_qkv(x1, b.tensor, n_rows, out, b.ptrs, b.sigs,
-                                    self.shard_table(st.numel), self.rank, self.world, src, lo,
-                                    b.next_epoch(), b.ag_counters, cos, sin, S, n_rot)
+        with self._peer_launch():
+            _native.cuda().fused_ag_qkv(x1, b.tensor, n_rows, out, b.ptrs, b.sigs,
+                                        self.shard_table(st.numel), self.rank, self.world, src, lo,
+                                        b.next_epoch(), b.ag_counters, cos, sin, S, n_rot)
         if rope is not None and not fuse_rope:
             cos, sin, S, n_q, n_kv, D = rope
             native.rope_qkv_(out, n_q, n_kv, D, cos, sin, S)

@@ -22,10 +22,14 @@ def test_fused_reduce_scatter_times_out_on_missing_peer(cuda_device):
     out = torch.empty(n // 2, dtype=torch.bfloat16, pin_memory=True)
     counter = torch.zeros(1, dtype=torch.int32, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
-    t0 = time.time()
-    C.fused_rs_d2h(ptrs, sigs, 0, 2, 0, n // 2, out, 0.5, 1, counter, err)
-    torch.cuda.synchronize()
-    dt = time.time() - t0
+    C.fused_set_peer_wait(2.0)  # default 60 s; a short limit keeps the test short
+    try:
+        t0 = time.time()
+        C.fused_rs_d2h(ptrs, sigs, 0, 2, 0, n // 2, out, 0.5, 1, counter, err)
+        torch.cuda.synchronize()
+        dt = time.time() - t0
+    finally:
+        C.fused_set_peer_wait(60.0)
     assert int(err.item()) == 201, "the ready-barrier wait should have expired"
     assert dt < 30
     # the context is still usable
