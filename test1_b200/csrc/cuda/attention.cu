@@ -485,6 +485,9 @@ static void check_qkv(const torch::Tensor& qkv, int64_t n_q, int64_t n_kv, int64
 std::vector<torch::Tensor> attention_fwd_tc(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                             int64_t S);
 std::vector<torch::Tensor> attention_fwd_tc2(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t S);
+void attention_bwd_pipe_core(torch::Tensor dout, torch::Tensor qkv, torch::Tensor lse,
+                             torch::Tensor delta, torch::Tensor dq_acc, torch::Tensor dqkv, int64_t n_q,
+                             int64_t n_kv, int64_t S);
 void attention_bwd_tc_core(torch::Tensor dout, torch::Tensor qkv, torch::Tensor lse,
                            torch::Tensor delta, torch::Tensor dq_acc, torch::Tensor dqkv, int64_t n_q,
                            int64_t n_kv, int64_t S);
@@ -509,6 +512,18 @@ void attn_set_mode(int64_t mode) {
 }
 
 int64_t attn_get_mode() { return attn_mode(); }
+
+// tcgen05 backward: pipelined (attention_bwd2.cu, the default) or the
+// serial one of attention_tc.cu (T1_ATTN_BWD_PIPE=0 / attn_set_bwd_pipelined).
+static bool& attn_bwd_pipelined() {
+  static bool on = [] {
+    const char* e = std::getenv("T1_ATTN_BWD_PIPE");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+void attn_set_bwd_pipelined(bool on) { attn_bwd_pipelined() = on; }
 
 std::vector<torch::Tensor> attention_fwd(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t D,
                                          int64_t S) {
@@ -556,7 +571,10 @@ torch::Tensor attention_bwd(torch::Tensor dout, torch::Tensor qkv, torch::Tensor
     check_launch("attention_bwd_delta");
   }
   if (attn_mode() >= 1) {
-    attention_bwd_tc_core(dout, qkv, lse, delta, dq_acc, dqkv, n_q, n_kv, S);
+    if (attn_bwd_pipelined())
+      attention_bwd_pipe_core(dout, qkv, lse, delta, dq_acc, dqkv, n_q, n_kv, S);
+    else
+      attention_bwd_tc_core(dout, qkv, lse, delta, dq_acc, dqkv, n_q, n_kv, S);
   } else {
     const int smem = 6 * attn::TILE_BYTES + 64 * 128 + 4 * 64 * 4;
     static bool cfg = false;

@@ -41,6 +41,7 @@ std::vector<torch::Tensor> attention_fwd_tc(torch::Tensor qkv, int64_t n_q, int6
                                             int64_t S);
 void attn_set_mode(int64_t mode);
 void attn_fwd2_set_poly(int64_t n);
+void attn_set_bwd_pipelined(bool on);
 void attn_fwd2_set_debug(torch::Tensor buf);
 std::vector<torch::Tensor> attention_fwd_tc2(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t S);
 int64_t attn_get_mode();
@@ -69,6 +70,7 @@ void multi_tensor_adam(int64_t chunk_size, torch::Tensor noop_flag,
 unsigned long long bounds_word_attention(bool);
 unsigned long long bounds_word_attention_tc(bool);
 unsigned long long bounds_word_attention_fwd2(bool);
+unsigned long long bounds_word_attention_bwd2(bool);
 unsigned long long bounds_word_elementwise(bool);
 unsigned long long bounds_word_embed_ce(bool);
 unsigned long long bounds_word_fused_adam(bool);
@@ -87,6 +89,7 @@ static std::vector<std::tuple<std::string, int64_t, int64_t>> bounds_errors(bool
       {"attention.cu", &t1::bounds_word_attention},
       {"attention_tc.cu", &t1::bounds_word_attention_tc},
       {"attention_fwd2.cu", &t1::bounds_word_attention_fwd2},
+      {"attention_bwd2.cu", &t1::bounds_word_attention_bwd2},
       {"elementwise.cu", &t1::bounds_word_elementwise},
       {"embed_ce.cu", &t1::bounds_word_embed_ce},
       {"fused_adam.cu", &t1::bounds_word_fused_adam},
@@ -146,6 +149,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_set_mode", &t1::attn_set_mode,
         "0: mma.sync, 1: tcgen05 (one query tile per CTA), 2: tcgen05 forward with two query tiles per CTA");
   m.def("attn_fwd2_set_poly", &t1::attn_fwd2_set_poly);
+  m.def("attn_set_bwd_pipelined", &t1::attn_set_bwd_pipelined, "tcgen05 backward: pipelined (default) or serial");
   m.def("attn_fwd2_set_debug", &t1::attn_fwd2_set_debug, "phase-stamp buffer of the two-tile forward (empty = off)");
   m.def("attention_fwd_tc2", &t1::attention_fwd_tc2);
   m.def("attn_get_mode", &t1::attn_get_mode);

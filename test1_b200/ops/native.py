@@ -98,6 +98,13 @@ def attn_set_mode(mode: int) -> None:
     _c().attn_set_mode(int(mode))
 
 
+def attn_set_bwd_pipelined(on: bool) -> None:
+    """tcgen05 attention backward: the pipelined kernel (default; Q
+    double-buffered, dQ drained while dK runs, the next scores computed
+    during the drain) or the serial one."""
+    _c().attn_set_bwd_pipelined(bool(on))
+
+
 def attn_fwd2_set_poly(n: int) -> None:
     """Two-tile forward: how many of every 8 exponentials run as a polynomial
     on the FMA pipe instead of the MUFU unit (0, 1 or 2)."""
