@@ -12,8 +12,9 @@
 //   MMA  dV += P^T dO   (commit do_free: dO's buffer may be reloaded)
 //        dQ  = dS K     into the dP columns (commit dq_ready)
 //        dK += dS^T Q   (commit q_free of Q's buffer)
-//   softmax warps: dQ * scale -> fp32 global accumulation (vector atomics),
-//        then arrive dq_free (the dP columns may be rewritten)
+//   softmax warps: dQ * scale -> fp32 global accumulation (TMA bulk
+//        reduce-adds of 32 x 32 boxes staged in shared memory), arriving
+//        dq_free as soon as the dP columns are read
 // What overlaps: Q is double-buffered and loaded ahead; dO is reloaded as
 // soon as dV has read it (while dQ and dK run); S of the next iteration is
 // computed while the softmax warps drain dQ, and the next dP as soon as the
@@ -27,6 +28,7 @@
 namespace t1 {
 
 CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_outer);
+CUtensorMap make_map_f32(const void* ptr, int64_t inner, int64_t outer, int64_t ld);
 torch::Tensor& gemm_error_word();
 
 namespace attn_bwd2 {
@@ -53,6 +55,10 @@ struct Params {
   bf16* dqkv;
   long ldd;
   int* err;
+  // optional phase stamps (clock64) of CTA (0, 0, 0): [it < 64][event < 8]
+  // of the softmax warp on TMEM lanes 0-31, [512 + it] the MMA issuer's
+  // wait for P/dS; nullptr = off
+  long long* dbg;
 };
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -72,7 +78,8 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int k) {
 
 __global__ void __launch_bounds__(192, 1)
     attn_bwd_pipe_kernel(const __grid_constant__ CUtensorMap tma_qkv,
-                         const __grid_constant__ CUtensorMap tma_do, const Params p) {
+                         const __grid_constant__ CUtensorMap tma_do,
+                         const __grid_constant__ CUtensorMap tma_dq, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -130,6 +137,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tensormap(&tma_qkv);
     prefetch_tensormap(&tma_do);
+    prefetch_tensormap(&tma_dq);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -200,11 +208,14 @@ __global__ void __launch_bounds__(192, 1)
         mma_commit(s_full);
         return true;
       };
+      long long* dbg = (p.dbg != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) ? p.dbg
+                                                                                                  : nullptr;
       bool ok = mbar_wait(kv_full, 0);
       if (!ok) err.set(246);
       if (ok && n_it > 0) ok = issue_s_dp(0);
       for (int it = 0; ok && it < n_it && !*abort_flag; ++it) {
         if (!mbar_wait(pds_full, it & 1)) { err.set(247); ok = false; break; }
+        if (dbg != nullptr && it < 64) dbg[512 + it] = clock64();
         tc_fence_after();
         const uint32_t q_addr = q0_addr + (it & 1) * TILE;
         // dV += P^T dO: dO's buffer is free afterwards
@@ -232,6 +243,11 @@ __global__ void __launch_bounds__(192, 1)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // row of the tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    long long* sdbg = (p.dbg != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 &&
+                       quarter == 0 && lane == 0) ? p.dbg : nullptr;
+    auto stamp = [&](int it, int e) {
+      if (sdbg != nullptr && it < 64) sdbg[it * 8 + e] = clock64();
+    };
     bool ok = true;
     auto wait_w = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
       int w = 0;
@@ -244,28 +260,54 @@ __global__ void __launch_bounds__(192, 1)
       }
       return __shfl_sync(0xffffffffu, w, 0) != 0;
     };
-    // dQ of iteration `it` (in the dP columns) -> global accumulation, then
-    // the dP columns are free for the next iteration
+    // dQ of iteration `it` (in the dP columns) x scale -> dq_acc by TMA bulk
+    // reduce-adds, staged through this warp's rows of the P buffer (free
+    // here: dV(it) has read P, and the softmax writes P(it + 1) only after
+    // the drain).  Per 64 columns two 32 x 32 fp32 boxes, 128B-swizzled: at
+    // sP + 4 KB q and sP + 16 KB + 4 KB q, exactly the bytes of P rows
+    // 32q .. 32q + 31 that this warp itself writes later.  One bulk reduce
+    // per box instead of 32 vector atomics per thread.
+    uint8_t* box_a = sP + quarter * 4096;
+    uint8_t* box_b = sP + BOX + quarter * 4096;
+    auto put_box = [&](uint8_t* box, const uint32_t (&u)[32]) {
+      uint8_t* rowp = box + lane * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+            make_float4(__uint_as_float(u[4 * j]) * p.scale, __uint_as_float(u[4 * j + 1]) * p.scale,
+                        __uint_as_float(u[4 * j + 2]) * p.scale, __uint_as_float(u[4 * j + 3]) * p.scale);
+    };
     auto drain_dq = [&](int it) {
       const int h = g * G + it / per_head;
-      const int qpos = (kb + it % per_head) * BM + r;
-      float* dst = p.dq_acc + (static_cast<long>(tok0 + qpos) * p.n_q + h) * D;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        tmem_ld_32x32b_x32(t_dp + lane_base + c * 32, u);
+      const int row0 = tok0 + (kb + it % per_head) * BM + quarter * 32;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t u0[32], u1[32];
+        tmem_ld_32x32b_x32(t_dp + lane_base + hh * 64, u0);
+        tmem_ld_32x32b_x32(t_dp + lane_base + hh * 64 + 32, u1);
         tmem_ld_wait();
-        if (qpos < p.S) {
-#pragma unroll
-          for (int v = 0; v < 8; ++v)
-            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + 4 * v),
-                      make_float4(__uint_as_float(u[4 * v]) * p.scale, __uint_as_float(u[4 * v + 1]) * p.scale,
-                                  __uint_as_float(u[4 * v + 2]) * p.scale, __uint_as_float(u[4 * v + 3]) * p.scale));
+        if (hh == 1) {
+          // every dP column is read: the next dP may be computed
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dq_free);
+          // and the first half's reduces have read the boxes
+          if (lane == 0) bulk_wait_group_read<0>();
+          __syncwarp();
+        }
+        put_box(box_a, u0);
+        put_box(box_b, u1);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tma_dq, box_a, h * D + hh * 64, row0);
+          tma_reduce_add_2d(&tma_dq, box_b, h * D + hh * 64 + 32, row0);
+          bulk_commit_group();
         }
       }
-      tc_fence_before();
+      // the boxes are rows of P: the reduces must have read them
+      if (lane == 0) bulk_wait_group_read<0>();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
     };
     for (int it = 0; it < n_it; ++it) {
       const int h = g * G + it / per_head;
@@ -274,12 +316,16 @@ __global__ void __launch_bounds__(192, 1)
       // issued before the drain below, so their latency hides behind it
       const float lse2 = q_ok ? p.lse[static_cast<long>(h) * p.T + tok0 + qpos] * LOG2E : 0.f;
       const float dlt = q_ok ? p.delta[static_cast<long>(h) * p.T + tok0 + qpos] : 0.f;
+      stamp(it, 0);
       if (it > 0) {
         if (!wait_w(dq_ready, (it - 1) & 1, 248)) { ok = false; break; }
+        stamp(it, 1);
         tc_fence_after();
         drain_dq(it - 1);
       }
+      stamp(it, 2);
       if (!wait_w(s_full, it & 1, 249)) { ok = false; break; }
+      stamp(it, 3);
       tc_fence_after();
       const int kbase = kb * BN;
 #pragma unroll
@@ -314,10 +360,12 @@ __global__ void __launch_bounds__(192, 1)
           *reinterpret_cast<uint4*>(sDS + off) = dk;
         }
       }
+      stamp(it, 4);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(pds_full);
+      stamp(it, 5);
     }
     if (ok && n_it > 0 && wait_w(dq_ready, (n_it - 1) & 1, 250)) {
       tc_fence_after();
@@ -357,6 +405,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
 
+  if (warp >= 2 && lane == 0) bulk_wait_group_all();  // the dQ reduce-adds landed
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -369,6 +418,22 @@ __global__ void __launch_bounds__(192, 1)
 
 T1_BOUNDS_READER(attention_bwd2)
 
+// Phase-stamp buffer (int64 [>= 576] on the GPU) or undefined = off.
+static torch::Tensor& attn_bwd2_debug() {
+  static torch::Tensor t;
+  return t;
+}
+
+void attn_bwd2_set_debug(torch::Tensor buf) {
+  if (buf.defined() && buf.numel() > 0) {
+    TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == torch::kInt64 && buf.is_contiguous() && buf.numel() >= 576,
+                "phase-stamp buffer must be a contiguous CUDA int64 tensor of >= 576 elements");
+    attn_bwd2_debug() = buf;
+  } else {
+    attn_bwd2_debug() = torch::Tensor();
+  }
+}
+
 // Pipelined backward core: same contract as attention_bwd_tc_core.
 void attention_bwd_pipe_core(torch::Tensor dout, torch::Tensor qkv, torch::Tensor lse,
                              torch::Tensor delta, torch::Tensor dq_acc, torch::Tensor dqkv, int64_t n_q,
@@ -376,6 +441,8 @@ void attention_bwd_pipe_core(torch::Tensor dout, torch::Tensor qkv, torch::Tenso
   const int64_t T = qkv.size(0), B = T / S;
   const CUtensorMap mq = make_map(qkv.data_ptr(), qkv.size(1), T, qkv.stride(0), 128);
   const CUtensorMap md = make_map(dout.data_ptr(), dout.size(1), T, dout.stride(0), 128);
+  TORCH_CHECK(dq_acc.is_contiguous() && dq_acc.numel() == T * n_q * attn_bwd2::D, "dq_acc must be [T, Hq, D]");
+  const CUtensorMap mdq = make_map_f32(dq_acc.data_ptr(), n_q * attn_bwd2::D, T, n_q * attn_bwd2::D);
   attn_bwd2::Params p;
   p.S = static_cast<int>(S);
   p.T = static_cast<int>(T);
@@ -389,6 +456,8 @@ void attention_bwd_pipe_core(torch::Tensor dout, torch::Tensor qkv, torch::Tenso
   p.dqkv = reinterpret_cast<__nv_bfloat16*>(dqkv.data_ptr());
   p.ldd = dqkv.stride(0);
   p.err = gemm_error_word().data_ptr<int>();
+  p.dbg = attn_bwd2_debug().defined() ? reinterpret_cast<long long*>(attn_bwd2_debug().data_ptr<int64_t>())
+                                      : nullptr;
   static bool cfg = false;
   if (!cfg) {
     T1_CHECK_CUDA(cudaFuncSetAttribute(attn_bwd2::attn_bwd_pipe_kernel,
@@ -396,7 +465,7 @@ void attention_bwd_pipe_core(torch::Tensor dout, torch::Tensor qkv, torch::Tenso
     cfg = true;
   }
   dim3 grid((S + attn_bwd2::BN - 1) / attn_bwd2::BN, n_kv, B);
-  attn_bwd2::attn_bwd_pipe_kernel<<<grid, 192, attn_bwd2::SMEM_BYTES, stream()>>>(mq, md, p);
+  attn_bwd2::attn_bwd_pipe_kernel<<<grid, 192, attn_bwd2::SMEM_BYTES, stream()>>>(mq, md, mdq, p);
   check_launch("attention_bwd_pipe");
   count_launch();
 }

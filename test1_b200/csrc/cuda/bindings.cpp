@@ -43,6 +43,7 @@ void attn_set_mode(int64_t mode);
 void attn_fwd2_set_poly(int64_t n);
 void attn_set_bwd_pipelined(bool on);
 void attn_fwd2_set_debug(torch::Tensor buf);
+void attn_bwd2_set_debug(torch::Tensor buf);
 std::vector<torch::Tensor> attention_fwd_tc2(torch::Tensor qkv, int64_t n_q, int64_t n_kv, int64_t S);
 int64_t attn_get_mode();
 torch::Tensor attention_bwd(torch::Tensor dout, torch::Tensor qkv, torch::Tensor out,
@@ -150,6 +151,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "0: mma.sync, 1: tcgen05 (one query tile per CTA), 2: tcgen05 forward with two query tiles per CTA");
   m.def("attn_fwd2_set_poly", &t1::attn_fwd2_set_poly);
   m.def("attn_set_bwd_pipelined", &t1::attn_set_bwd_pipelined, "tcgen05 backward: pipelined (default) or serial");
+  m.def("attn_bwd2_set_debug", &t1::attn_bwd2_set_debug, "phase-stamp buffer of the pipelined backward (empty = off)");
   m.def("attn_fwd2_set_debug", &t1::attn_fwd2_set_debug, "phase-stamp buffer of the two-tile forward (empty = off)");
   m.def("attention_fwd_tc2", &t1::attention_fwd_tc2);
   m.def("attn_get_mode", &t1::attn_get_mode);

@@ -84,6 +84,24 @@ CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld,
   return m;
 }
 
+// 2-D fp32 tensor map, 128B swizzle, box = 32 x 32 (one 128-byte row per
+// box row): `inner` contiguous elements per row, `outer` rows, `ld` elements
+// between rows.  Used for bulk reduce-adds into fp32 accumulators.
+CUtensorMap make_map_f32(const void* ptr, int64_t inner, int64_t outer, int64_t ld) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "fp32 tensor must be 16-byte aligned");
+  TORCH_CHECK((ld * 4) % 16 == 0 && inner % 32 == 0, "fp32 rows must be multiples of 32 elements");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 4)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (fp32) failed with ", (int)r);
+  return m;
+}
+
 torch::Tensor& gemm_error_word() {
   static thread_local std::unordered_map<int, torch::Tensor> words;
   int dev = 0;

@@ -96,6 +96,16 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 2-D tiled bulk tensor reduce-add shared -> global (bulk-group completion):
+// the box is added element-wise into the tensor (fp32 adds in L2).
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
 // 1-D bulk copy global -> shared of this CTA (no multicast), completion
 // counted in bytes on `bar`; both addresses 16-byte aligned, size a
 // multiple of 16.
