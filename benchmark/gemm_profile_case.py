@@ -1,8 +1,10 @@
 """One GEMM shape, a few launches: the small case for an ncu capture of the
 tcgen05 GEMM (Llama-3.1-8B QKV projection: 4096 x 6144 x 4096, ~130 MB of
 operands).  Usage: python benchmark/gemm_profile_case.py [fwd|dgrad|wgrad] [--pair | --pair-tma]
-(--pair: CTA pairs with the register-store epilogue; --pair-tma: CTA pairs
-with the shared-memory + TMA-store epilogue)."""
+[--shape qkv|o|down] (--pair: CTA pairs with the register-store epilogue;
+--pair-tma: CTA pairs with the shared-memory + TMA-store epilogue, the
+default; --shape: the QKV (default), O (4096^3, a stream-K tail) or down
+(4096 x 4096 x 14336) projection)."""
 import os
 import sys
 
@@ -18,7 +20,8 @@ def main() -> None:
         native.gemm_set_mode(2)
     elif "--pair" in sys.argv:
         native.gemm_set_mode(1)
-    M, N, K = 4096, 6144, 4096
+    shape = sys.argv[sys.argv.index("--shape") + 1] if "--shape" in sys.argv else "qkv"
+    M, N, K = {"qkv": (4096, 6144, 4096), "o": (4096, 4096, 4096), "down": (4096, 4096, 14336)}[shape]
     x = torch.randn(M, K, device="cuda").bfloat16()
     w = torch.randn(N, K, device="cuda").bfloat16()
     dy = torch.randn(M, N, device="cuda").bfloat16()
