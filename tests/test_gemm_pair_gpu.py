@@ -79,7 +79,8 @@ def test_pair_wgrad_accumulate(pair_mode, M, N, K):
     assert _rel(out, expect) < 6e-3
 
 
-@pytest.mark.parametrize("T,S,n_q,n_kv,K", [(4096, 1024, 32, 8, 4096), (300, 100, 4, 2, 512)])
+@pytest.mark.parametrize("T,S,n_q,n_kv,K", [(4096, 1024, 32, 8, 4096), (300, 100, 4, 2, 512),
+                                             (1024, 1024, 32, 8, 4096)])  # last: 96 tiles, stream-K tail
 def test_qkv_gemm_with_fused_rope(T, S, n_q, n_kv, K):
     """QKV projection with the rotary embedding applied in the TMA-store
     epilogue (fp32 accumulator rotated before the bf16 rounding) against the
