@@ -18,7 +18,10 @@ the host bandwidth is known.  Bytes per parameter per step:
 step of the Llama-3.1-8B config measured ~190 GB/s on the B200 box).  The
 printed step times are predictions, not measurements.  Against the measured
 config-2 steps (full mode) at 190 GB/s: 1 GPU 1.35 s predicted / 1.40-1.48 s
-measured, 2 GPUs 1.52 / 1.54, 4 GPUs 1.86 / 1.78.  Shard mode at 2 GPUs
+measured, 2 GPUs 1.52 / 1.53-1.54, 4 GPUs 1.86 / 1.78, 8 GPUs 2.43 / 2.48.  Shard
+mode at 8 GPUs with 8192 tokens per GPU (config 3) measured 1.66 s against 1.35 s
+of host traffic: there the GPU work per step (twice the tokens, activation
+offload) is no longer hidden entirely.  Shard mode at 2 GPUs
 measured 1.77 s against 1.35 predicted: there each layer's fused gather sits
 on the forward's critical path (it feeds the QKV GEMM directly instead of
 being prefetched a layer ahead), a latency this traffic model leaves out.
